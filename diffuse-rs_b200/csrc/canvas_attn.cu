@@ -1,0 +1,446 @@
+// canvas_attn.cu -- the single translation unit of libcanvas_attn.so: the
+// sm_100a kernels (attn_fwd.cuh, prep.cuh) and the C ABI declared in
+// include/canvas_attn.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "canvas_attn.h"
+#include "attn_fwd.cuh"
+#include "prep.cuh"
+
+namespace ca {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// ---------------------------------------------------------------- driver entry
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D bf16 view [tokens][heads][hd] (innermost first in TMA order), boxes of
+// 64 x box_heads x box_tokens with 128-byte swizzle; out-of-range reads fill 0.
+int make_tmap(CUtensorMap* m, const void* base, int64_t hd, int64_t heads, int64_t tokens,
+              int64_t row_stride_elems, uint32_t box_heads, uint32_t box_tokens) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return CA_ERR_CUDA;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(tokens)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(hd) * 2,
+                           static_cast<cuuint64_t>(row_stride_elems) * 2};
+  cuuint32_t box[3] = {64, box_heads, box_tokens};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CA_OK : CA_ERR_INVALID;
+}
+
+// ---------------------------------------------------------------- launch
+template <class C>
+int launch_cfg(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+               const FwdParams& p, int n_qtiles, cudaStream_t st) {
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmemBytes) != cudaSuccess)
+      return CA_ERR_CUDA;
+    attr_done[dev] = true;
+  }
+  dim3 grid(n_qtiles, p.n_head_kv, p.batch);
+  attn_fwd_kernel<C><<<grid, 256, C::kSmemBytes, st>>>(tq, tk, tv, p);
+  return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
+}
+
+using Cfg64 = FwdCfg<64, 128, 3>;
+using Cfg128 = FwdCfg<128, 128, 2>;
+using Cfg192 = FwdCfg<192, 64, 2>;
+using Cfg256 = FwdCfg<256, 64, 2>;
+
+int block_n_for(int hdp) { return hdp <= 128 ? 128 : 64; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int clamp_opt(int64_t v) {  // Option<usize> as int32 (None = -1)
+  if (v < 0) return -1;
+  return v > INT_MAX ? INT_MAX : static_cast<int>(v);
+}
+
+}  // namespace
+
+// Validates a device-args struct and launches the attention kernel.
+int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
+  if (!a || !a->q || !a->k || !a->v || !a->out) return CA_ERR_INVALID;
+  const int H = a->n_head, Hkv = a->n_head_kv, hd = a->head_dim;
+  if (H <= 0 || Hkv <= 0 || hd <= 0 || a->batch < 0) return CA_ERR_INVALID;
+  if (H % Hkv != 0) return CA_ERR_INVALID;
+  if (hd % 8 != 0 || hd > 256) return CA_ERR_UNSUPPORTED;
+  const int G = H / Hkv;
+  if (G > 128) return CA_ERR_UNSUPPORTED;
+  if (a->batch == 0) return CA_OK;
+  const bool varlen = a->cu_q != nullptr || a->cu_k != nullptr;
+  if (varlen && (!a->cu_q || !a->cu_k || a->total_q < 0 || a->total_k < 0 || a->max_sq < 0))
+    return CA_ERR_INVALID;
+  if (!varlen && (a->sq < 0 || a->sk < 0)) return CA_ERR_INVALID;
+  const int64_t total_q = varlen ? a->total_q : static_cast<int64_t>(a->batch) * a->sq;
+  const int64_t total_k = varlen ? a->total_k : static_cast<int64_t>(a->batch) * a->sk;
+  const int max_sq = varlen ? a->max_sq : a->sq;
+  const int64_t max_sk = varlen ? total_k : a->sk;
+  if (total_q == 0 || max_sq == 0) return CA_OK;
+  if (total_q > INT_MAX || total_k > INT_MAX) return CA_ERR_UNSUPPORTED;
+  const int64_t qrs = a->q_row_stride ? a->q_row_stride : static_cast<int64_t>(H) * hd;
+  const int64_t krs = a->kv_row_stride ? a->kv_row_stride : static_cast<int64_t>(Hkv) * hd;
+  const int64_t ors = a->out_row_stride ? a->out_row_stride : static_cast<int64_t>(H) * hd;
+  if (qrs < static_cast<int64_t>(H) * hd || krs < static_cast<int64_t>(Hkv) * hd ||
+      ors < static_cast<int64_t>(H) * hd)
+    return CA_ERR_INVALID;
+  // TMA: 16-byte aligned bases and strides; epilogue: 16-byte output vectors.
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out) ||
+      qrs % 8 || krs % 8 || ors % (a->out_f32 ? 4 : 8))
+    return CA_ERR_INVALID;
+
+  const int hdp = (hd + 63) / 64 * 64;
+  const int bn = block_n_for(hdp);
+  const int64_t n_kt = (max_sk + bn - 1) / bn;
+  if (n_kt > Cfg128::kMaxTiles) return CA_ERR_UNSUPPORTED;
+
+  FwdParams p{};
+  p.out = a->out;
+  p.out_f32 = a->out_f32 ? 1 : 0;
+  p.out_row_stride = ors;
+  p.batch = a->batch;
+  p.sq = a->sq;
+  p.sk = a->sk;
+  p.cu_q = a->cu_q;
+  p.cu_k = a->cu_k;
+  p.n_head = H;
+  p.n_head_kv = Hkv;
+  p.G = G;
+  p.hd = hd;
+  p.QT = 128 / G;
+  p.R = p.QT * G;
+  p.q_pos = a->q_pos;
+  p.k_pos = a->k_pos;
+  p.q_seq = a->q_seq;
+  p.k_seq = a->k_seq;
+  p.q_prefix = a->q_prefix;
+  p.window = a->sliding_window < 0 ? kNoWindow
+                                   : static_cast<int>(a->sliding_window >= INT_MAX
+                                                          ? INT_MAX - 1
+                                                          : a->sliding_window);
+  p.causal_prefix = clamp_opt(a->causal_prefix);
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.softcap = a->softcap > 0.f ? a->softcap : 0.f;
+  p.any_mask = (a->q_pos || a->k_pos || a->q_seq || a->k_seq || a->q_prefix ||
+                p.window != kNoWindow || p.causal_prefix >= 0)
+                   ? 1
+                   : 0;
+
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = make_tmap(&tq, a->q, hd, H, total_q, qrs, G, p.QT)) != CA_OK) return rc;
+  if ((rc = make_tmap(&tk, a->k, hd, Hkv, total_k == 0 ? 1 : total_k, krs, 1, bn)) != CA_OK)
+    return rc;
+  if ((rc = make_tmap(&tv, a->v, hd, Hkv, total_k == 0 ? 1 : total_k, krs, 1, bn)) != CA_OK)
+    return rc;
+  const int n_qtiles = (max_sq + p.QT - 1) / p.QT;
+  if (hdp == 64) return launch_cfg<Cfg64>(tq, tk, tv, p, n_qtiles, st);
+  if (hdp == 128) return launch_cfg<Cfg128>(tq, tk, tv, p, n_qtiles, st);
+  if (hdp == 192) return launch_cfg<Cfg192>(tq, tk, tv, p, n_qtiles, st);
+  return launch_cfg<Cfg256>(tq, tk, tv, p, n_qtiles, st);
+}
+
+}  // namespace ca
+
+namespace ca {
+namespace {
+
+int block_impl(const ca_block_args* a, cudaStream_t st) {
+  if (!a || !a->q || !a->k || !a->v || !a->active_pos || !a->rope || !a->cache_k ||
+      !a->cache_v || !a->q_work || !a->out)
+    return CA_ERR_INVALID;
+  const int H = a->n_head, Hkv = a->n_head_kv, hd = a->head_dim;
+  if (a->batch < 0 || a->n_active < 0 || a->n_total < a->n_active || H <= 0 || Hkv <= 0 ||
+      hd <= 0 || H % Hkv)
+    return CA_ERR_INVALID;
+  if (a->rope_dim < 0 || a->rope_dim > hd || a->rope_dim % 2 || a->rope_len <= 0)
+    return CA_ERR_INVALID;
+  if (a->batch == 0 || a->n_active == 0) return CA_OK;
+  PrepParams pp{};
+  pp.q = static_cast<const __nv_bfloat16*>(a->q);
+  pp.k = static_cast<const __nv_bfloat16*>(a->k);
+  pp.v = static_cast<const __nv_bfloat16*>(a->v);
+  pp.pos = a->active_pos;
+  pp.q_norm_w = a->q_norm_w;
+  pp.k_norm_w = a->k_norm_w;
+  pp.v_norm = a->v_norm;
+  pp.eps = a->rms_eps;
+  pp.rope = a->rope;
+  pp.rope_len = a->rope_len;
+  pp.rope_dim = a->rope_dim;
+  pp.q_out = static_cast<__nv_bfloat16*>(a->q_work);
+  pp.cache_k = static_cast<__nv_bfloat16*>(a->cache_k);
+  pp.cache_v = static_cast<__nv_bfloat16*>(a->cache_v);
+  pp.batch = a->batch;
+  pp.na = a->n_active;
+  pp.n_total = a->n_total;
+  pp.H = H;
+  pp.Hkv = Hkv;
+  pp.hd = hd;
+  const long long jobs = static_cast<long long>(a->batch) * a->n_active * (H + 2 * Hkv);
+  const int blocks = static_cast<int>(std::min<long long>((jobs + 7) / 8, 148LL * 16));
+  prep_block_kernel<<<blocks, 256, 8 * hd * sizeof(float), st>>>(pp);
+  if (cudaGetLastError() != cudaSuccess) return CA_ERR_CUDA;
+
+  ca_dev_args d{};
+  d.q = a->q_work;
+  d.k = a->cache_k;
+  d.v = a->cache_v;
+  d.out = a->out;
+  d.out_f32 = a->out_f32;
+  d.batch = a->batch;
+  d.sq = a->n_active;
+  d.sk = a->n_total;
+  d.n_head = H;
+  d.n_head_kv = Hkv;
+  d.head_dim = hd;
+  d.q_pos = a->active_pos;  // keys are positions 0..n_total-1 in order: k_pos = identity
+  d.sliding_window = a->sliding_window;
+  d.causal_prefix = a->causal_prefix;
+  d.scale = a->scale;
+  d.softcap = a->softcap;
+  return attention_dev_impl(&d, st);
+}
+
+// Library-owned device buffers of the host-buffer entry point, one set per
+// device, grown on demand and kept for the process lifetime.
+struct HostCtx {
+  std::mutex mu;
+  cudaStream_t stream = nullptr;
+  void* buf = nullptr;
+  size_t cap = 0;
+};
+HostCtx g_host[kMaxDevices];
+
+size_t align_up(size_t x) { return (x + 255) / 256 * 256; }
+
+int host_f32_impl(float* out, const float* q, const float* k, const float* v, const ca_shape* s,
+                  const ca_rows* qr, const ca_rows* kr) {
+  if (!out || !q || !k || !v || !s || !qr || !kr) return CA_ERR_INVALID;
+  if (s->nq < 0 || s->nk < 0 || s->n_head <= 0 || s->n_head_kv <= 0 || s->head_dim <= 0 ||
+      s->n_head % s->n_head_kv)
+    return CA_ERR_INVALID;
+  if (s->nq == 0) return CA_OK;
+  if ((s->nq > 0 && !qr->pos) || (s->nk > 0 && !kr->pos)) return CA_ERR_INVALID;
+  if (s->nq > INT_MAX || s->nk > INT_MAX) return CA_ERR_UNSUPPORTED;
+  const bool qseq = qr->seq && qr->n_seq > 0, kseq = kr->seq && kr->n_seq > 0;
+  const bool qpre = qr->prefix && qr->n_prefix > 0;
+  if ((qseq && qr->n_seq < static_cast<size_t>(s->nq)) ||
+      (kseq && kr->n_seq < static_cast<size_t>(s->nk)) ||
+      (qpre && qr->n_prefix < static_cast<size_t>(s->nq)))
+    return CA_ERR_INVALID;
+  // Row metadata to int32 on the host; positions and ids must fit.
+  const int64_t nq = s->nq, nk = s->nk;
+  std::vector<int32_t> meta;
+  meta.reserve(3 * nq + 2 * nk);
+  auto push = [&](const int64_t* src, int64_t n, bool is_prefix) -> bool {
+    for (int64_t i = 0; i < n; ++i) {
+      int64_t x = src[i];
+      if (x < 0) return false;
+      if (x > INT_MAX) {
+        if (!is_prefix) return false;
+        x = INT_MAX;
+      }
+      meta.push_back(static_cast<int32_t>(x));
+    }
+    return true;
+  };
+  // Positions are usize: they must fit int32 here.
+  if (!push(qr->pos, nq, false) || !push(kr->pos, nk, false)) return CA_ERR_UNSUPPORTED;
+  const size_t off_qseq = meta.size();
+  if (qseq && !push(qr->seq, nq, false)) return CA_ERR_UNSUPPORTED;
+  const size_t off_kseq = meta.size();
+  if (kseq && !push(kr->seq, nk, false)) return CA_ERR_UNSUPPORTED;
+  const size_t off_qpre = meta.size();
+  if (qpre && !push(qr->prefix, nq, true)) return CA_ERR_UNSUPPORTED;
+  // A single non-empty seq side compares against id 0 on the other side.
+  std::vector<int32_t> zeros;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return CA_ERR_CUDA;
+  HostCtx& c = g_host[dev];
+  std::lock_guard<std::mutex> lock(c.mu);
+  if (!c.stream && cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking) != cudaSuccess)
+    return CA_ERR_CUDA;
+  const int64_t qe = nq * s->n_head * s->head_dim, ke = nk * s->n_head_kv * s->head_dim;
+  const size_t b_qf = align_up(qe * 4), b_kf = align_up(ke * 4);
+  const size_t b_qh = align_up(qe * 2), b_kh = align_up(ke * 2);
+  const size_t b_meta = align_up(meta.size() * 4 + 4 * (nq + nk));
+  // Layout: [q f32 | k f32 | v f32 | q bf16 | k bf16 | v bf16 | meta]; out reuses q f32.
+  const size_t need = b_qf + 2 * b_kf + b_qh + 2 * b_kh + b_meta;
+  if (need > c.cap) {
+    if (c.buf) cudaFree(c.buf);
+    c.buf = nullptr;
+    c.cap = 0;
+    if (cudaMalloc(&c.buf, need) != cudaSuccess) return CA_ERR_NOMEM;
+    c.cap = need;
+  }
+  char* base = static_cast<char*>(c.buf);
+  float* dq = reinterpret_cast<float*>(base);
+  float* dk = reinterpret_cast<float*>(base + b_qf);
+  float* dv = reinterpret_cast<float*>(base + b_qf + b_kf);
+  __nv_bfloat16* hq = reinterpret_cast<__nv_bfloat16*>(base + b_qf + 2 * b_kf);
+  __nv_bfloat16* hk = reinterpret_cast<__nv_bfloat16*>(base + b_qf + 2 * b_kf + b_qh);
+  __nv_bfloat16* hv = reinterpret_cast<__nv_bfloat16*>(base + b_qf + 2 * b_kf + b_qh + b_kh);
+  int32_t* dmeta = reinterpret_cast<int32_t*>(base + b_qf + 2 * b_kf + b_qh + 2 * b_kh);
+  int32_t* dzero = dmeta + meta.size();
+  cudaStream_t st = c.stream;
+  bool ok = cudaMemcpyAsync(dq, q, qe * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+  ok = ok && cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+  ok = ok && cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+  ok = ok && cudaMemcpyAsync(dmeta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, st) ==
+                 cudaSuccess;
+  if ((qseq != kseq) && ok)
+    ok = cudaMemsetAsync(dzero, 0, 4 * (nq + nk), st) == cudaSuccess;
+  if (!ok) return CA_ERR_CUDA;
+  auto conv = [&](const float* src, __nv_bfloat16* dst, long long n) {
+    const int blocks = static_cast<int>(std::min<long long>((n / 4 + 255) / 256 + 1, 148 * 8));
+    f32_to_bf16_kernel<<<blocks, 256, 0, st>>>(src, dst, n);
+  };
+  conv(dq, hq, qe);
+  if (ke > 0) {
+    conv(dk, hk, ke);
+    conv(dv, hv, ke);
+  }
+  ca_dev_args d{};
+  d.q = hq;
+  d.k = hk;
+  d.v = hv;
+  d.out = dq;  // fp32 output overwrites the fp32 Q staging copy
+  d.out_f32 = 1;
+  d.batch = 1;
+  d.sq = static_cast<int32_t>(nq);
+  d.sk = static_cast<int32_t>(nk);
+  d.n_head = static_cast<int32_t>(s->n_head);
+  d.n_head_kv = static_cast<int32_t>(s->n_head_kv);
+  d.head_dim = static_cast<int32_t>(s->head_dim);
+  if (s->head_dim > INT_MAX) return CA_ERR_UNSUPPORTED;
+  d.q_pos = dmeta;
+  d.k_pos = dmeta + nq;
+  d.q_seq = qseq ? dmeta + off_qseq : (kseq ? dzero : nullptr);
+  d.k_seq = kseq ? dmeta + off_kseq : (qseq ? dzero : nullptr);
+  d.q_prefix = qpre ? dmeta + off_qpre : nullptr;
+  d.sliding_window = s->sliding_window;
+  d.causal_prefix = s->causal_prefix;
+  d.scale = s->scale;
+  d.softcap = s->softcap;
+  int rc = nk == 0 ? CA_OK : attention_dev_impl(&d, st);
+  if (rc != CA_OK) return rc;
+  if (nk == 0) {  // no key at all: every row is 0 * (1 / 0)
+    std::vector<float> nan(qe, std::nanf(""));
+    std::memcpy(out, nan.data(), qe * 4);
+    return cudaStreamSynchronize(st) == cudaSuccess ? CA_OK : CA_ERR_CUDA;
+  }
+  if (cudaMemcpyAsync(out, dq, qe * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return CA_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return CA_ERR_CUDA;
+  int derr = 0;
+  if (cudaMemcpyFromSymbol(&derr, g_device_error, sizeof(int)) != cudaSuccess) return CA_ERR_CUDA;
+  if (derr != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    return CA_ERR_TIMEOUT;
+  }
+  return CA_OK;
+}
+
+}  // namespace
+}  // namespace ca
+
+extern "C" {
+
+int ca_attention_host_f32(float* out, const float* q, const float* k, const float* v,
+                          const ca_shape* s, const ca_rows* qr, const ca_rows* kr) {
+  return ca::host_f32_impl(out, q, k, v, s, qr, kr);
+}
+
+int ca_attention_dev(const ca_dev_args* a, void* stream) {
+  return ca::attention_dev_impl(a, static_cast<cudaStream_t>(stream));
+}
+
+int ca_attention_block_dev(const ca_block_args* a, void* stream) {
+  return ca::block_impl(a, static_cast<cudaStream_t>(stream));
+}
+
+// build_rope_cache_ff (src/model/ops.rs:398-416): freq_i = 1 / theta^(2i/d)
+// in f32, divided by freq_factors[i] when given; entry t*half+i = sin_cos(t*freq).
+int ca_build_rope_table(float* out, int64_t max_seq_len, int64_t rope_dim, float theta,
+                        const float* freq_factors) {
+  if (!out || max_seq_len < 0 || rope_dim < 0 || rope_dim % 2) return CA_ERR_INVALID;
+  const int64_t half = rope_dim / 2;
+  std::vector<float> freq(half);
+  for (int64_t i = 0; i < half; ++i) {
+    float f = 1.0f / powf(theta, 2.0f * static_cast<float>(i) / static_cast<float>(rope_dim));
+    if (freq_factors) f /= freq_factors[i];
+    freq[i] = f;
+  }
+  for (int64_t t = 0; t < max_seq_len; ++t)
+    for (int64_t i = 0; i < half; ++i) {
+      const float x = static_cast<float>(t) * freq[i];
+      out[2 * (t * half + i)] = sinf(x);
+      out[2 * (t * half + i) + 1] = cosf(x);
+    }
+  return CA_OK;
+}
+
+int ca_device_status(void* stream) {
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return CA_ERR_CUDA;
+  int derr = 0;
+  if (cudaMemcpyFromSymbol(&derr, ca::g_device_error, sizeof(int)) != cudaSuccess)
+    return CA_ERR_CUDA;
+  if (derr == 0) return CA_OK;
+  const int zero = 0;
+  cudaMemcpyToSymbol(ca::g_device_error, &zero, sizeof(int));
+  return derr;
+}
+
+const char* ca_status_string(int status) {
+  switch (status) {
+    case CA_OK: return "ok";
+    case CA_ERR_INVALID: return "invalid argument";
+    case CA_ERR_UNSUPPORTED: return "unsupported by this build";
+    case CA_ERR_CUDA: return "CUDA error";
+    case CA_ERR_TIMEOUT: return "device-side wait timed out";
+    case CA_ERR_NOMEM: return "out of memory";
+    default: return "unknown status";
+  }
+}
+
+const char* ca_version(void) { return "canvas_attn 0.1.0 sm_100a"; }
+
+}  // extern "C"

@@ -1,0 +1,188 @@
+/*
+ * canvas_attn.h -- C ABI of the B200 canvas-attention library
+ * (libcanvas_attn.so, built from diffuse-rs_b200/csrc/).
+ *
+ * Drop-in boundary for diffuse-rs's attention path. Each entry point names the
+ * reference interface it replaces. Plain pointers and sizes only; no C++ or
+ * torch types. All functions return CA_OK (0) or a negative ca_status and
+ * never abort the process.
+ *
+ * Layouts are the reference's (src/model/attention.rs:101-106), row-major:
+ *   Q   [tokens, n_head, head_dim]
+ *   K,V [tokens, n_head_kv, head_dim]
+ *   out [tokens, n_head * head_dim]
+ * GQA maps query head h to kv head h / (n_head / n_head_kv)
+ * (src/model/attention.rs:149).
+ */
+#ifndef CANVAS_ATTN_H
+#define CANVAS_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    CA_OK = 0,
+    CA_ERR_INVALID = -1,     /* bad shape, null pointer, inconsistent sizes */
+    CA_ERR_UNSUPPORTED = -2, /* valid for the reference, not for this build (e.g. head_dim > 256) */
+    CA_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed */
+    CA_ERR_TIMEOUT = -4,     /* a bounded device-side wait expired; outputs are undefined */
+    CA_ERR_NOMEM = -5        /* device or pinned allocation failed */
+} ca_status;
+
+/* Mirrors AttnShape (src/model/attention.rs:10-27). Option<usize> fields use
+ * -1 for None. softcap is an extension with no reference counterpart:
+ * 0 = off, else score <- softcap * tanh(score * scale / softcap). */
+typedef struct {
+    int64_t nq;
+    int64_t nk;
+    int64_t n_head;
+    int64_t n_head_kv;
+    int64_t head_dim;
+    int64_t sliding_window; /* key visible iff |qpos - kpos| < window; -1 = None */
+    int64_t causal_prefix;  /* query rows with qpos < prefix see kpos <= qpos; -1 = None */
+    float scale;
+    float softcap;
+} ca_shape;
+
+/* Mirrors Rows (src/model/attention.rs:65-77). pos has one entry per row.
+ * seq / prefix may be NULL with length 0, which means the reference's empty
+ * slice: every row in sequence 0 / the shape's scalar causal_prefix. */
+typedef struct {
+    const int64_t* pos;
+    const int64_t* seq;
+    size_t n_seq;
+    const int64_t* prefix;
+    size_t n_prefix;
+} ca_rows;
+
+/*
+ * ca_attention_host_f32 -- replaces
+ *   fn attention(out: &mut [f32], q: &[f32], k: &[f32], v: &[f32],
+ *                s: AttnShape, qr: Rows, kr: Rows)
+ *   (src/model/attention.rs:106), called at src/model/forward.rs:343.
+ * Host fp32 buffers in and out, synchronous. Operands are rounded to bf16 on
+ * the GPU (fp32 accumulation); masking is exactly visible()
+ * (src/model/attention.rs:35-57). A query row with no visible key gets NaN,
+ * as the reference's acc * (1 / 0) does. Uses GPU `device` of the calling
+ * thread's current device; serialised by an internal lock.
+ */
+int ca_attention_host_f32(float* out, const float* q, const float* k, const float* v,
+                          const ca_shape* s, const ca_rows* qr, const ca_rows* kr);
+
+/* Device-resident arguments for ca_attention_dev (all pointers are device
+ * pointers). Q/K/V are bf16. Sequences are either uniform
+ * (cu_q == cu_k == NULL: batch sequences of sq queries and sk keys, stored
+ * back to back) or varlen (cu_q/cu_k: int32 [batch + 1] row offsets, max_sq
+ * bounds every sequence's query count). */
+typedef struct {
+    const void* q;  /* bf16 [total_q, n_head, head_dim]; token stride q_row_stride */
+    const void* k;  /* bf16 [total_k, n_head_kv, head_dim]; stride kv_row_stride */
+    const void* v;  /* bf16, same layout as k */
+    void* out;      /* [total_q, n_head, head_dim]; stride out_row_stride */
+    int32_t out_f32; /* 1: fp32 output, 0: bf16 output */
+    int64_t q_row_stride;   /* elements between tokens; 0 = n_head * head_dim */
+    int64_t kv_row_stride;  /* 0 = n_head_kv * head_dim */
+    int64_t out_row_stride; /* 0 = n_head * head_dim */
+    int32_t batch;
+    int32_t sq;
+    int32_t sk;
+    const int32_t* cu_q;
+    const int32_t* cu_k;
+    int32_t max_sq;  /* varlen only: largest per-sequence query count */
+    int64_t total_q; /* varlen only: rows in q/out (cu_q[batch]) */
+    int64_t total_k; /* varlen only: rows in k/v (cu_k[batch]) */
+    int32_t n_head;
+    int32_t n_head_kv;
+    int32_t head_dim;
+    const int32_t* q_pos;    /* per global row; NULL = row index within its sequence */
+    const int32_t* k_pos;
+    const int32_t* q_seq;    /* per global row sequence id; NULL = all 0 */
+    const int32_t* k_seq;
+    const int32_t* q_prefix; /* per global query row; NULL = causal_prefix */
+    int64_t sliding_window;  /* -1 = None */
+    int64_t causal_prefix;   /* -1 = None */
+    float scale;
+    float softcap;           /* 0 = off (extension) */
+} ca_dev_args;
+
+/*
+ * ca_attention_dev -- the device-resident form of attention()
+ * (src/model/attention.rs:106-133): bf16 operands in HBM, fp32 accumulation,
+ * asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream).
+ * Batch is a grid dimension; varlen segments stand for the reference's
+ * concatenated block-diagonal rows (src/model/forward.rs:113-160).
+ * Allocates nothing. head_dim must be a multiple of 8 and <= 256.
+ */
+int ca_attention_dev(const ca_dev_args* a, void* stream);
+
+/* Arguments of the fused attention block (pre-ops + cache + attention). */
+typedef struct {
+    const void* q;   /* bf16 [batch, n_active, n_head, head_dim], post-projection, pre-norm */
+    const void* k;   /* bf16 [batch, n_active, n_head_kv, head_dim] */
+    const void* v;   /* bf16 [batch, n_active, n_head_kv, head_dim] */
+    int32_t batch;
+    int32_t n_active;
+    const int32_t* active_pos; /* int32 [batch, n_active] sequence positions */
+    const float* q_norm_w;     /* fp32 [head_dim] or NULL (no q-norm) */
+    const float* k_norm_w;     /* fp32 [head_dim] or NULL */
+    int32_t v_norm;            /* 1: unweighted per-head RMSNorm of V (Gemma) */
+    float rms_eps;
+    const float* rope;         /* fp32 [rope_len, rope_dim/2, 2] (sin, cos) table */
+    int32_t rope_len;
+    int32_t rope_dim;          /* rotated dims per head (partial rotary), even */
+    void* cache_k;             /* bf16 [batch, n_total, n_head_kv, head_dim] */
+    void* cache_v;
+    int32_t n_total;           /* positions per sequence; keys = all n_total positions */
+    void* q_work;              /* bf16 [batch, n_active, n_head, head_dim] scratch (caller-owned) */
+    void* out;                 /* [batch, n_active, n_head, head_dim] */
+    int32_t out_f32;
+    int32_t n_head;
+    int32_t n_head_kv;
+    int32_t head_dim;
+    int64_t sliding_window;
+    int64_t causal_prefix;
+    float scale;
+    float softcap;
+} ca_block_args;
+
+/*
+ * ca_attention_block_dev -- replaces the attention half of
+ * Model::attention_block, src/model/forward.rs:296-343: per-head QK RMSNorm
+ * (ops.rs:385-389, :107-114) -> optional V noscale norm (forward.rs:304-308)
+ * -> NeoX RoPE at each row's position (ops.rs:420-452) -> StepCache::store of
+ * post-RoPE K/V (cache.rs:62-70) -> attention over every cached position
+ * (cache.rs:73-81 gather and forward.rs:312-317 concat become in-place reads:
+ * after the store, cached ∪ active positions are exactly 0..n_total-1, so the
+ * cache in position order is the key set). Active positions must be distinct
+ * and every cached position must hold K/V stored by an earlier call.
+ * Asynchronous on `stream`; allocates nothing.
+ */
+int ca_attention_block_dev(const ca_block_args* a, void* stream);
+
+/*
+ * ca_build_rope_table -- replaces build_rope_cache_ff (src/model/ops.rs:398-416),
+ * host side, run once at load like the reference. out: host fp32
+ * [max_seq_len, rope_dim/2, 2] as (sin, cos); freq_factors may be NULL.
+ */
+int ca_build_rope_table(float* out, int64_t max_seq_len, int64_t rope_dim, float theta,
+                        const float* freq_factors);
+
+/* Reads and clears the device-side error word of the current device after
+ * synchronising `stream`: CA_OK, or CA_ERR_TIMEOUT if a kernel's bounded wait
+ * expired since the last call. */
+int ca_device_status(void* stream);
+
+/* Human-readable text of a ca_status. */
+const char* ca_status_string(int status);
+
+/* Library version, "canvas_attn <major>.<minor>.<patch> sm_100a". */
+const char* ca_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CANVAS_ATTN_H */

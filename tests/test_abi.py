@@ -1,0 +1,88 @@
+"""The C-ABI library loads, exports every symbol include/canvas_attn.h
+declares, and validates arguments -- all without a GPU (no compute calls)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+import canvas_attn as ca
+from oracle import oracle as orc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "canvas_attn.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ca_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_and_mirror_agree():
+    assert declared_symbols() == sorted(ca.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(ca.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_status_strings():
+    assert "sm_100a" in ca.version()
+    assert ca.status_string(ca.CA_OK) == "ok"
+    assert "timed out" in ca.status_string(ca.CA_ERR_TIMEOUT)
+
+
+def test_rope_table_matches_oracle_bit_exact():
+    # build_rope_cache_ff (src/model/ops.rs:398-416): same f32 formula.
+    for theta, dim in ((500000.0, 128), (1e6, 128), (10000.0, 256), (50000.0, 64)):
+        a = ca.build_rope_cache(300, dim, theta)
+        b = orc.build_rope_cache(300, dim, theta)
+        np.testing.assert_array_equal(a, b)
+    ff = np.linspace(1.0, 4.0, 32).astype(np.float32)
+    np.testing.assert_array_equal(ca.build_rope_cache(50, 64, 1e4, ff),
+                                  orc.build_rope_cache(50, 64, 1e4, ff))
+
+
+def test_dev_entry_rejects_bad_arguments_without_touching_the_gpu():
+    a = ca.make_dev_args(None, None, None, None, batch=1, sq=1, sk=1, n_head=1, n_head_kv=1,
+                         head_dim=128)
+    assert ca.lib.ca_attention_dev(ctypes.byref(a), None) == ca.CA_ERR_INVALID
+    # Unsupported head_dim / GQA ratio / misaligned pointers are rejected up front.
+    fake = 1 << 40
+    a = ca.make_dev_args(fake, fake, fake, fake, batch=1, sq=4, sk=4, n_head=2, n_head_kv=1,
+                         head_dim=300)
+    assert ca.lib.ca_attention_dev(ctypes.byref(a), None) == ca.CA_ERR_UNSUPPORTED
+    a = ca.make_dev_args(fake, fake, fake, fake, batch=1, sq=4, sk=4, n_head=3, n_head_kv=2,
+                         head_dim=128)
+    assert ca.lib.ca_attention_dev(ctypes.byref(a), None) == ca.CA_ERR_INVALID
+    a = ca.make_dev_args(fake + 2, fake, fake, fake, batch=1, sq=4, sk=4, n_head=2,
+                         n_head_kv=1, head_dim=128)
+    assert ca.lib.ca_attention_dev(ctypes.byref(a), None) == ca.CA_ERR_INVALID
+    # Empty batches are a no-op success.
+    a = ca.make_dev_args(fake, fake, fake, fake, batch=0, sq=4, sk=4, n_head=2, n_head_kv=1,
+                         head_dim=128)
+    assert ca.lib.ca_attention_dev(ctypes.byref(a), None) == ca.CA_OK
+
+
+def test_block_entry_rejects_bad_arguments():
+    a = ca.make_block_args(None, None, None, batch=1, n_active=1, active_pos=None, rope=None,
+                           rope_len=1, rope_dim=2, cache_k=None, cache_v=None, n_total=1,
+                           q_work=None, out=None, n_head=1, n_head_kv=1, head_dim=8)
+    assert ca.lib.ca_attention_block_dev(ctypes.byref(a), None) == ca.CA_ERR_INVALID
+
+
+def test_host_entry_validates_shape():
+    s = ca.AttnShape(nq=2, nk=2, n_head=3, n_head_kv=2, head_dim=8)
+    out = np.zeros(2 * 3 * 8, np.float32)
+    q = np.zeros(2 * 3 * 8, np.float32)
+    k = np.zeros(2 * 2 * 8, np.float32)
+    cs = s.to_c()
+    cq, _k1 = ca.Rows([0, 1]).to_c()
+    ck, _k2 = ca.Rows([0, 1]).to_c()
+    rc = ca.lib.ca_attention_host_f32(out.ctypes.data, q.ctypes.data, k.ctypes.data,
+                                      k.ctypes.data, ctypes.byref(cs), ctypes.byref(cq),
+                                      ctypes.byref(ck))
+    assert rc == ca.CA_ERR_INVALID
