@@ -74,7 +74,8 @@ class CaDevArgs(ctypes.Structure):
                 ("k_pos", ctypes.c_void_p), ("q_seq", ctypes.c_void_p),
                 ("k_seq", ctypes.c_void_p), ("q_prefix", ctypes.c_void_p),
                 ("sliding_window", ctypes.c_int64), ("causal_prefix", ctypes.c_int64),
-                ("scale", ctypes.c_float), ("softcap", ctypes.c_float)]
+                ("scale", ctypes.c_float), ("softcap", ctypes.c_float),
+                ("precise", ctypes.c_int32)]
 
 
 class CaBlockArgs(ctypes.Structure):
@@ -90,7 +91,7 @@ class CaBlockArgs(ctypes.Structure):
                 ("n_head", ctypes.c_int32), ("n_head_kv", ctypes.c_int32),
                 ("head_dim", ctypes.c_int32), ("sliding_window", ctypes.c_int64),
                 ("causal_prefix", ctypes.c_int64), ("scale", ctypes.c_float),
-                ("softcap", ctypes.c_float)]
+                ("softcap", ctypes.c_float), ("precise", ctypes.c_int32)]
 
 
 def _load():
@@ -222,7 +223,8 @@ def make_dev_args(q, k, v, out, *, batch, sq, sk, n_head, n_head_kv, head_dim,
                   out_f32=False, cu_q=None, cu_k=None, max_sq=0, total_q=0, total_k=0,
                   q_pos=None, k_pos=None, q_seq=None, k_seq=None, q_prefix=None,
                   sliding_window=None, causal_prefix=None, scale=1.0, softcap=0.0,
-                  q_row_stride=0, kv_row_stride=0, out_row_stride=0) -> CaDevArgs:
+                  q_row_stride=0, kv_row_stride=0, out_row_stride=0,
+                  precise=False) -> CaDevArgs:
     return CaDevArgs(_ptr(q), _ptr(k), _ptr(v), _ptr(out), 1 if out_f32 else 0,
                      q_row_stride, kv_row_stride, out_row_stride, batch, sq, sk,
                      _ptr(cu_q), _ptr(cu_k), max_sq, total_q, total_k,
@@ -230,7 +232,7 @@ def make_dev_args(q, k, v, out, *, batch, sq, sk, n_head, n_head_kv, head_dim,
                      _ptr(k_seq), _ptr(q_prefix),
                      -1 if sliding_window is None else int(sliding_window),
                      -1 if causal_prefix is None else int(causal_prefix),
-                     float(scale), float(softcap))
+                     float(scale), float(softcap), 1 if precise else 0)
 
 
 def attention_dev(q, k, v, out, *, stream=None, **kw) -> None:
@@ -247,14 +249,14 @@ def make_block_args(q, k, v, *, batch, n_active, active_pos, rope, rope_len, rop
                     cache_k, cache_v, n_total, q_work, out, n_head, n_head_kv, head_dim,
                     q_norm_w=None, k_norm_w=None, v_norm=False, rms_eps=1e-6,
                     out_f32=False, sliding_window=None, causal_prefix=None, scale=1.0,
-                    softcap=0.0) -> CaBlockArgs:
+                    softcap=0.0, precise=False) -> CaBlockArgs:
     return CaBlockArgs(_ptr(q), _ptr(k), _ptr(v), batch, n_active, _ptr(active_pos),
                        _ptr(q_norm_w), _ptr(k_norm_w), 1 if v_norm else 0, float(rms_eps),
                        _ptr(rope), rope_len, rope_dim, _ptr(cache_k), _ptr(cache_v), n_total,
                        _ptr(q_work), _ptr(out), 1 if out_f32 else 0, n_head, n_head_kv,
                        head_dim, -1 if sliding_window is None else int(sliding_window),
                        -1 if causal_prefix is None else int(causal_prefix), float(scale),
-                       float(softcap))
+                       float(softcap), 1 if precise else 0)
 
 
 def attention_block_dev(*args, stream=None, **kw) -> None:

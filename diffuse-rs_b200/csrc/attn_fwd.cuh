@@ -56,18 +56,23 @@ struct FwdParams {
   int any_mask;       // any of: positions, seq ids, prefixes, window, causal prefix
 };
 
-template <int HDP_, int BN_, int ST_>
+template <int HDP_, int BN_, int ST_, bool PRECISE_ = false>
 struct FwdCfg {
   static constexpr int HDP = HDP_;  // head_dim padded to a multiple of 64
   static constexpr int BN = BN_;    // keys per tile
   static constexpr int ST = ST_;    // K/V pipeline stages
+  // PRECISE: P is split into bf16 hi + lo terms (two PV MMAs), so the softmax
+  // weights reach the tensor core with ~16 significant bits instead of 8.
+  static constexpr bool PRECISE = PRECISE_;
+  static constexpr int kPTerms = PRECISE ? 2 : 1;
   static constexpr int kChunks = HDP / 64;  // 128-byte swizzle atoms along head_dim
   static constexpr int kQChunk = 128 * 128;
   static constexpr int kKChunk = BN * 128;
   static constexpr int kPChunk = 128 * 128;
   static constexpr int kQBytes = kChunks * kQChunk;
   static constexpr int kKVBytes = kChunks * kKChunk;
-  static constexpr int kPBytes = (BN / 64) * kPChunk;
+  static constexpr int kPBytes = kPTerms * (BN / 64) * kPChunk;
+  static constexpr int kPTermBytes = (BN / 64) * kPChunk;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;
   static constexpr int kOffV = kOffK + ST * kKVBytes;
@@ -83,7 +88,8 @@ struct FwdCfg {
   static constexpr int kBarO = kBarP + 1;
   static constexpr int kBarF = kBarO + 1;
   static constexpr int kNumBars = kBarF + 1;
-  static constexpr int kMaxTiles = 1024;
+  // Largest key-tile count per sequence (keys <= kMaxTiles * BN).
+  static constexpr int kMaxTiles = (PRECISE && HDP == 256) ? 512 : 1024;
   static constexpr int kOffList = kOffBar + kNumBars * 8;
   static constexpr int kOffFlags = kOffList + kMaxTiles * 2;
   static constexpr int kOffMisc = kOffFlags + kMaxTiles;
@@ -345,10 +351,14 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_after();
         const uint32_t vbase = sV + s * C::kKVBytes;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(sP + (kk >> 2) * C::kPChunk + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(vbase + kk * 2048, C::kKChunk, 1024);
-          umma_ss(tmem + C::kOCol, a, bd, C::kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
+        for (int term = 0; term < C::kPTerms; ++term) {
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t a = umma_desc_sw128(
+                sP + term * C::kPTermBytes + (kk >> 2) * C::kPChunk + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(vbase + kk * 2048, C::kKChunk, 1024);
+            umma_ss(tmem + C::kOCol, a, bd, C::kIdescO, (i > 0 || kk > 0 || term > 0) ? 1u : 0u);
+          }
         }
         umma_commit(bar(C::kBarO));
         umma_commit(bar(C::kBarE + s));
@@ -453,6 +463,7 @@ __global__ void __launch_bounds__(256, 1)
       const float mu = (m == -INFINITY) ? 0.f : m;
       float sum = 0.f;
       uint32_t pk[BN / 2];
+      uint32_t pl[C::PRECISE ? BN / 2 : 1];
 #pragma unroll
       for (int i = 0; i < BN; i += 2) {
         float p0, p1;
@@ -465,6 +476,11 @@ __global__ void __launch_bounds__(256, 1)
         }
         sum += p0 + p1;
         pk[i / 2] = pack_bf16(p0, p1);
+        if constexpr (C::PRECISE) {
+          const float h0 = __uint_as_float(pk[i / 2] << 16);
+          const float h1 = __uint_as_float(pk[i / 2] & 0xffff0000u);
+          pl[i / 2] = pack_bf16(p0 - h0, p1 - h1);
+        }
       }
       l = l * corr + sum;
 
@@ -496,6 +512,8 @@ __global__ void __launch_bounds__(256, 1)
           const uint32_t addr = sP + cc * C::kPChunk + r * 128 + ((u ^ (r & 7)) << 4);
           const int w0 = cc * 32 + u * 4;
           st_shared_v4(addr, pk[w0], pk[w0 + 1], pk[w0 + 2], pk[w0 + 3]);
+          if constexpr (C::PRECISE)
+            st_shared_v4(addr + C::kPTermBytes, pl[w0], pl[w0 + 1], pl[w0 + 2], pl[w0 + 3]);
         }
       }
       fence_proxy_async_smem();

@@ -59,29 +59,42 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t hd, int64_t heads, int64
 }
 
 // ---------------------------------------------------------------- launch
-template <class C>
-int launch_cfg(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-               const FwdParams& p, int n_qtiles, cudaStream_t st) {
-  static bool attr_done[kMaxDevices] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
-  if (!attr_done[dev]) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::kSmemBytes) != cudaSuccess)
-      return CA_ERR_CUDA;
-    attr_done[dev] = true;
+// Builds the tensor maps for one tile configuration and launches it.
+struct Launch {
+  const ca_dev_args* a;
+  const FwdParams* p;
+  int64_t total_q, total_k;
+  int max_sq;
+  int64_t max_sk;
+  int64_t qrs, krs;
+  cudaStream_t st;
+
+  template <class C>
+  int run() const {
+    static bool attr_done[kMaxDevices] = {};
+    const int64_t n_kt = (max_sk + C::BN - 1) / C::BN;
+    if (n_kt > C::kMaxTiles) return CA_ERR_UNSUPPORTED;
+    CUtensorMap tq, tk, tv;
+    const int hd = p->hd;
+    const int64_t tk_rows = total_k == 0 ? 1 : total_k;
+    int rc;
+    if ((rc = make_tmap(&tq, a->q, hd, p->n_head, total_q, qrs, p->G, p->QT)) != CA_OK) return rc;
+    if ((rc = make_tmap(&tk, a->k, hd, p->n_head_kv, tk_rows, krs, 1, C::BN)) != CA_OK) return rc;
+    if ((rc = make_tmap(&tv, a->v, hd, p->n_head_kv, tk_rows, krs, 1, C::BN)) != CA_OK) return rc;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
+    if (!attr_done[dev]) {
+      if (cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::kSmemBytes) != cudaSuccess)
+        return CA_ERR_CUDA;
+      attr_done[dev] = true;
+    }
+    const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
+    dim3 grid(n_qtiles, p->n_head_kv, p->batch);
+    attn_fwd_kernel<C><<<grid, 256, C::kSmemBytes, st>>>(tq, tk, tv, *p);
+    return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
   }
-  dim3 grid(n_qtiles, p.n_head_kv, p.batch);
-  attn_fwd_kernel<C><<<grid, 256, C::kSmemBytes, st>>>(tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
-}
-
-using Cfg64 = FwdCfg<64, 128, 3>;
-using Cfg128 = FwdCfg<128, 128, 2>;
-using Cfg192 = FwdCfg<192, 64, 2>;
-using Cfg256 = FwdCfg<256, 64, 2>;
-
-int block_n_for(int hdp) { return hdp <= 128 ? 128 : 64; }
+};
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -124,9 +137,6 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
     return CA_ERR_INVALID;
 
   const int hdp = (hd + 63) / 64 * 64;
-  const int bn = block_n_for(hdp);
-  const int64_t n_kt = (max_sk + bn - 1) / bn;
-  if (n_kt > Cfg128::kMaxTiles) return CA_ERR_UNSUPPORTED;
 
   FwdParams p{};
   p.out = a->out;
@@ -161,18 +171,17 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
                    ? 1
                    : 0;
 
-  CUtensorMap tq, tk, tv;
-  int rc;
-  if ((rc = make_tmap(&tq, a->q, hd, H, total_q, qrs, G, p.QT)) != CA_OK) return rc;
-  if ((rc = make_tmap(&tk, a->k, hd, Hkv, total_k == 0 ? 1 : total_k, krs, 1, bn)) != CA_OK)
-    return rc;
-  if ((rc = make_tmap(&tv, a->v, hd, Hkv, total_k == 0 ? 1 : total_k, krs, 1, bn)) != CA_OK)
-    return rc;
-  const int n_qtiles = (max_sq + p.QT - 1) / p.QT;
-  if (hdp == 64) return launch_cfg<Cfg64>(tq, tk, tv, p, n_qtiles, st);
-  if (hdp == 128) return launch_cfg<Cfg128>(tq, tk, tv, p, n_qtiles, st);
-  if (hdp == 192) return launch_cfg<Cfg192>(tq, tk, tv, p, n_qtiles, st);
-  return launch_cfg<Cfg256>(tq, tk, tv, p, n_qtiles, st);
+  Launch L{a, &p, total_q, total_k, max_sq, max_sk, qrs, krs, st};
+  if (a->precise) {
+    if (hdp == 64) return L.run<FwdCfg<64, 128, 3, true>>();
+    if (hdp == 128) return L.run<FwdCfg<128, 64, 3, true>>();
+    if (hdp == 192) return L.run<FwdCfg<192, 64, 2, true>>();
+    return L.run<FwdCfg<256, 64, 2, true>>();
+  }
+  if (hdp == 64) return L.run<FwdCfg<64, 128, 3>>();
+  if (hdp == 128) return L.run<FwdCfg<128, 128, 2>>();
+  if (hdp == 192) return L.run<FwdCfg<192, 64, 2>>();
+  return L.run<FwdCfg<256, 64, 2>>();
 }
 
 }  // namespace ca
@@ -234,6 +243,7 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   d.causal_prefix = a->causal_prefix;
   d.scale = a->scale;
   d.softcap = a->softcap;
+  d.precise = a->precise;
   return attention_dev_impl(&d, st);
 }
 
@@ -297,12 +307,18 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
   std::lock_guard<std::mutex> lock(c.mu);
   if (!c.stream && cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking) != cudaSuccess)
     return CA_ERR_CUDA;
-  const int64_t qe = nq * s->n_head * s->head_dim, ke = nk * s->n_head_kv * s->head_dim;
+  if (s->head_dim > 4096) return CA_ERR_UNSUPPORTED;
+  const int hd = static_cast<int>(s->head_dim);
+  const int hd_p = (hd + 7) / 8 * 8;  // TMA rows must be 16-byte multiples
+  const int64_t qe = nq * s->n_head * hd, ke = nk * s->n_head_kv * hd;
+  const int64_t qe_p = nq * s->n_head * hd_p, ke_p = nk * s->n_head_kv * hd_p;
   const size_t b_qf = align_up(qe * 4), b_kf = align_up(ke * 4);
-  const size_t b_qh = align_up(qe * 2), b_kh = align_up(ke * 2);
+  const size_t b_qh = align_up(qe_p * 2), b_kh = align_up(ke_p * 2);
+  const size_t b_out = hd_p == hd ? 0 : align_up(qe_p * 4);
   const size_t b_meta = align_up(meta.size() * 4 + 4 * (nq + nk));
-  // Layout: [q f32 | k f32 | v f32 | q bf16 | k bf16 | v bf16 | meta]; out reuses q f32.
-  const size_t need = b_qf + 2 * b_kf + b_qh + 2 * b_kh + b_meta;
+  // Layout: [q f32 | k f32 | v f32 | q bf16 | k bf16 | v bf16 | out f32 | meta].
+  // With no padding the fp32 output overwrites the fp32 Q staging copy.
+  const size_t need = b_qf + 2 * b_kf + b_qh + 2 * b_kh + b_out + b_meta;
   if (need > c.cap) {
     if (c.buf) cudaFree(c.buf);
     c.buf = nullptr;
@@ -311,45 +327,52 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
     c.cap = need;
   }
   char* base = static_cast<char*>(c.buf);
-  float* dq = reinterpret_cast<float*>(base);
-  float* dk = reinterpret_cast<float*>(base + b_qf);
-  float* dv = reinterpret_cast<float*>(base + b_qf + b_kf);
-  __nv_bfloat16* hq = reinterpret_cast<__nv_bfloat16*>(base + b_qf + 2 * b_kf);
-  __nv_bfloat16* hk = reinterpret_cast<__nv_bfloat16*>(base + b_qf + 2 * b_kf + b_qh);
-  __nv_bfloat16* hv = reinterpret_cast<__nv_bfloat16*>(base + b_qf + 2 * b_kf + b_qh + b_kh);
-  int32_t* dmeta = reinterpret_cast<int32_t*>(base + b_qf + 2 * b_kf + b_qh + 2 * b_kh);
+  size_t off = 0;
+  auto carve = [&](size_t bytes) { char* r = base + off; off += bytes; return r; };
+  float* dq = reinterpret_cast<float*>(carve(b_qf));
+  float* dk = reinterpret_cast<float*>(carve(b_kf));
+  float* dv = reinterpret_cast<float*>(carve(b_kf));
+  __nv_bfloat16* hq = reinterpret_cast<__nv_bfloat16*>(carve(b_qh));
+  __nv_bfloat16* hk = reinterpret_cast<__nv_bfloat16*>(carve(b_kh));
+  __nv_bfloat16* hv = reinterpret_cast<__nv_bfloat16*>(carve(b_kh));
+  float* dout = b_out ? reinterpret_cast<float*>(carve(b_out)) : dq;
+  int32_t* dmeta = reinterpret_cast<int32_t*>(carve(b_meta));
   int32_t* dzero = dmeta + meta.size();
   cudaStream_t st = c.stream;
   bool ok = cudaMemcpyAsync(dq, q, qe * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
-  ok = ok && cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
-  ok = ok && cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+  ok = ok && (ke == 0 || cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess);
+  ok = ok && (ke == 0 || cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess);
   ok = ok && cudaMemcpyAsync(dmeta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, st) ==
                  cudaSuccess;
   if ((qseq != kseq) && ok)
     ok = cudaMemsetAsync(dzero, 0, 4 * (nq + nk), st) == cudaSuccess;
   if (!ok) return CA_ERR_CUDA;
-  auto conv = [&](const float* src, __nv_bfloat16* dst, long long n) {
-    const int blocks = static_cast<int>(std::min<long long>((n / 4 + 255) / 256 + 1, 148 * 8));
-    f32_to_bf16_kernel<<<blocks, 256, 0, st>>>(src, dst, n);
+  auto conv = [&](const float* src, __nv_bfloat16* dst, long long n, long long n_p) {
+    const int blocks = static_cast<int>(std::min<long long>((n_p / 4 + 255) / 256 + 1, 148 * 8));
+    if (hd_p == hd)
+      f32_to_bf16_kernel<<<blocks, 256, 0, st>>>(src, dst, n);
+    else
+      f32_to_bf16_pad_kernel<<<blocks, 256, 0, st>>>(src, dst, n / hd, hd, hd_p);
   };
-  conv(dq, hq, qe);
+  conv(dq, hq, qe, qe_p);
   if (ke > 0) {
-    conv(dk, hk, ke);
-    conv(dv, hv, ke);
+    conv(dk, hk, ke, ke_p);
+    conv(dv, hv, ke, ke_p);
   }
+  if (cudaGetLastError() != cudaSuccess) return CA_ERR_CUDA;
   ca_dev_args d{};
   d.q = hq;
   d.k = hk;
   d.v = hv;
-  d.out = dq;  // fp32 output overwrites the fp32 Q staging copy
+  d.out = dout;
   d.out_f32 = 1;
+  d.precise = 1;
   d.batch = 1;
   d.sq = static_cast<int32_t>(nq);
   d.sk = static_cast<int32_t>(nk);
   d.n_head = static_cast<int32_t>(s->n_head);
   d.n_head_kv = static_cast<int32_t>(s->n_head_kv);
-  d.head_dim = static_cast<int32_t>(s->head_dim);
-  if (s->head_dim > INT_MAX) return CA_ERR_UNSUPPORTED;
+  d.head_dim = hd_p;
   d.q_pos = dmeta;
   d.k_pos = dmeta + nq;
   d.q_seq = qseq ? dmeta + off_qseq : (kseq ? dzero : nullptr);
@@ -366,8 +389,13 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
     std::memcpy(out, nan.data(), qe * 4);
     return cudaStreamSynchronize(st) == cudaSuccess ? CA_OK : CA_ERR_CUDA;
   }
-  if (cudaMemcpyAsync(out, dq, qe * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+  if (hd_p == hd) {
+    if (cudaMemcpyAsync(out, dout, qe * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+      return CA_ERR_CUDA;
+  } else if (cudaMemcpy2DAsync(out, hd * 4, dout, hd_p * 4, hd * 4, nq * s->n_head,
+                               cudaMemcpyDeviceToHost, st) != cudaSuccess) {
     return CA_ERR_CUDA;
+  }
   if (cudaStreamSynchronize(st) != cudaSuccess) return CA_ERR_CUDA;
   int derr = 0;
   if (cudaMemcpyFromSymbol(&derr, g_device_error, sizeof(int)) != cudaSuccess) return CA_ERR_CUDA;

@@ -114,4 +114,18 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* 
     out[i] = __float2bfloat16_rn(in[i]);
 }
 
+// fp32 [rows, hd] -> bf16 [rows, hd_p] with zero columns hd..hd_p-1, for
+// head dims that are not a multiple of 8 (TMA rows must be 16-byte multiples).
+__global__ void f32_to_bf16_pad_kernel(const float* __restrict__ in,
+                                       __nv_bfloat16* __restrict__ out, long long rows, int hd,
+                                       int hd_p) {
+  const long long n = rows * hd_p;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / hd_p;
+    const int c = static_cast<int>(i - r * hd_p);
+    out[i] = __float2bfloat16_rn(c < hd ? in[r * hd + c] : 0.f);
+  }
+}
+
 }  // namespace ca

@@ -64,11 +64,14 @@ typedef struct {
  *   fn attention(out: &mut [f32], q: &[f32], k: &[f32], v: &[f32],
  *                s: AttnShape, qr: Rows, kr: Rows)
  *   (src/model/attention.rs:106), called at src/model/forward.rs:343.
- * Host fp32 buffers in and out, synchronous. Operands are rounded to bf16 on
- * the GPU (fp32 accumulation); masking is exactly visible()
+ * Host fp32 buffers in and out, synchronous. Q/K/V are rounded to bf16 on
+ * the GPU (fp32 accumulation, softmax weights in the precise two-term form;
+ * head_dim is zero-padded to a multiple of 8 internally); masking is exactly
+ * visible()
  * (src/model/attention.rs:35-57). A query row with no visible key gets NaN,
- * as the reference's acc * (1 / 0) does. Uses GPU `device` of the calling
- * thread's current device; serialised by an internal lock.
+ * as the reference's acc * (1 / 0) does. Runs on the calling thread's
+ * current CUDA device; calls are serialised per device by an internal lock,
+ * and device buffers are kept (and grown) between calls.
  */
 int ca_attention_host_f32(float* out, const float* q, const float* k, const float* v,
                           const ca_shape* s, const ca_rows* qr, const ca_rows* kr);
@@ -107,6 +110,9 @@ typedef struct {
     int64_t causal_prefix;   /* -1 = None */
     float scale;
     float softcap;           /* 0 = off (extension) */
+    int32_t precise;         /* 1: softmax weights enter the PV product as two bf16
+                                terms (hi + lo), ~2x the PV tensor work, error
+                                ~256x smaller; 0: one bf16 term (fastest) */
 } ca_dev_args;
 
 /*
@@ -147,6 +153,7 @@ typedef struct {
     int64_t causal_prefix;
     float scale;
     float softcap;
+    int32_t precise;           /* as ca_dev_args.precise */
 } ca_block_args;
 
 /*

@@ -1,0 +1,183 @@
+"""GPU parity of the reference-shaped entry points: the host fp32 drop-in
+(`attention()`, src/model/attention.rs:106) on every golden case and on
+reference-style row metadata, and the fused attention block
+(src/model/forward.rs:296-343) with and without an inter-step cache."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import canvas_attn as ca
+from helpers import bf16_round, check_close, oracle_attention, randn
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def golden_cases():
+    z = np.load(os.path.join(GOLD, "attention_cases.npz"))
+    names = sorted({k.split("/")[0] for k in z.files})
+    return {n: {k.split("/")[1]: z[k] for k in z.files if k.startswith(n + "/")} for n in names}
+
+
+CASES = golden_cases()
+
+
+def host_call(c, q, k, v):
+    nq, nk, h, hkv, hd = (int(x) for x in c["dims"])
+    win, cp = int(c["window"]), int(c["causal_prefix"])
+    s = ca.AttnShape(nq, nk, h, hkv, hd, None if win < 0 else win, None if cp < 0 else cp,
+                     float(c["scale"]), float(c["softcap"]))
+    qr = ca.Rows(c["q_pos"], c.get("qseq", []), c.get("qprefix", []))
+    kr = ca.Rows(c["k_pos"], c.get("kseq", []))
+    out = np.zeros(nq * h * hd, np.float32)
+    ca.attention(out, q, k, v, s, qr, kr)
+    return out
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_host_entry_on_golden_cases(name):
+    c = CASES[name]
+    nq, nk, h, hkv, hd = (int(x) for x in c["dims"])
+    if hd > 256:
+        # head_dim 320 is valid for the reference, unsupported by this build.
+        with pytest.raises(ca.CaError) as e:
+            host_call(c, c["q"], c["k"], c["v"])
+        assert e.value.status == ca.CA_ERR_UNSUPPORTED
+        return
+    q, k, v = (bf16_round(torch.from_numpy(c[x])).numpy() for x in ("q", "k", "v"))
+    got = host_call(c, q, k, v)
+    win, cp = int(c["window"]), int(c["causal_prefix"])
+    ref = orc.attention(q, k, v, nq=nq, nk=nk, n_head=h, n_head_kv=hkv, head_dim=hd,
+                        q_pos=c["q_pos"], k_pos=c["k_pos"], q_seq=c.get("qseq"),
+                        k_seq=c.get("kseq"), q_prefix=c.get("qprefix"),
+                        sliding_window=None if win < 0 else win,
+                        causal_prefix=None if cp < 0 else cp, scale=float(c["scale"]),
+                        softcap=float(c["softcap"]))
+    check_close(got, ref, h, hd, what=name)
+    if name == "uniform_scores":  # reference known answer [2, 4] (tests.rs:104-114)
+        assert abs(got[0] - 2.0) < 1e-6 and abs(got[1] - 4.0) < 1e-6
+
+
+def test_host_entry_block_diagonal_seq_ids_large():
+    # Three sequences concatenated with seq ids and per-sequence positions,
+    # plus Gemma-style per-row causal prefixes (forward.rs:153-160).
+    rng = np.random.default_rng(21)
+    lens = [150, 260, 90]
+    H, Hkv, hd = 4, 2, 128
+    pos = np.concatenate([np.arange(n) for n in lens])
+    seq = np.concatenate([np.full(n, i) for i, n in enumerate(lens)])
+    canvas_start = [40, 100, 0]
+    prefix = np.array([canvas_start[s] for s in seq])
+    n = len(pos)
+    q = bf16_round(torch.from_numpy(rng.standard_normal(n * H * hd).astype(np.float32))).numpy()
+    k = bf16_round(torch.from_numpy(rng.standard_normal(n * Hkv * hd).astype(np.float32))).numpy()
+    v = bf16_round(torch.from_numpy(rng.standard_normal(n * Hkv * hd).astype(np.float32))).numpy()
+    s = ca.AttnShape(n, n, H, Hkv, hd, scale=hd ** -0.5)
+    out = np.zeros(n * H * hd, np.float32)
+    ca.attention(out, q, k, v, s, ca.Rows(pos, seq, prefix), ca.Rows(pos, seq))
+    ref = orc.attention(q, k, v, nq=n, nk=n, n_head=H, n_head_kv=Hkv, head_dim=hd, q_pos=pos,
+                        k_pos=pos, q_seq=seq, k_seq=seq, q_prefix=prefix, scale=hd ** -0.5)
+    check_close(out, ref, H, hd, what="block-diagonal + prefix")
+
+
+def _oracle_block(q, k, v, pos, wq, wk, rope, rope_dim, h, hkv, hd, eps):
+    """Reference op order (forward.rs:296-310) on fp32 copies. The attention
+    operands (post-RoPE Q/K) are then rounded to bf16, as the GPU's are: the
+    parity protocol is bf16 operands with fp32 accumulation."""
+    q = orc.norm_heads(q, wq, eps) if wq is not None else q.copy()
+    k = orc.norm_heads(k, wk, eps) if wk is not None else k.copy()
+    q = orc.rotate_rows(q, rope, pos, h, hd, rope_dim)
+    k = orc.rotate_rows(k, rope, pos, hkv, hd, rope_dim)
+    rb = lambda x: bf16_round(torch.from_numpy(x)).numpy()  # noqa: E731
+    return rb(q), rb(k), v
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_block_without_cache(qk_norm):
+    B, S, H, Hkv, hd = 2, 300, 4, 4, 128
+    eps, theta = 1e-6, 50000.0
+    g = torch.Generator().manual_seed(31)
+    q = bf16_round(randn(g, B, S, H, hd))
+    k = bf16_round(randn(g, B, S, Hkv, hd))
+    v = bf16_round(randn(g, B, S, Hkv, hd))
+    wq = torch.rand(hd, generator=g) + 0.5 if qk_norm else None
+    wk = torch.rand(hd, generator=g) + 0.5 if qk_norm else None
+    rope = ca.build_rope_cache(4096, hd, theta)
+    pos = torch.arange(S, dtype=torch.int32).repeat(B, 1)
+    dev = dict(q=q.to(torch.bfloat16).cuda(), k=k.to(torch.bfloat16).cuda(),
+               v=v.to(torch.bfloat16).cuda())
+    cache_k = torch.zeros(B, S, Hkv, hd, dtype=torch.bfloat16, device="cuda")
+    cache_v = torch.zeros_like(cache_k)
+    q_work = torch.empty(B, S, H, hd, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(B, S, H, hd, device="cuda")
+    rope_d = torch.from_numpy(rope).cuda()
+    ca.attention_block_dev(dev["q"], dev["k"], dev["v"], batch=B, n_active=S,
+                           active_pos=pos.cuda(), rope=rope_d, rope_len=4096, rope_dim=hd,
+                           cache_k=cache_k, cache_v=cache_v, n_total=S, q_work=q_work, out=out,
+                           n_head=H, n_head_kv=Hkv, head_dim=hd,
+                           q_norm_w=None if wq is None else wq.cuda(),
+                           k_norm_w=None if wk is None else wk.cuda(), rms_eps=eps,
+                           out_f32=True, scale=hd ** -0.5, precise=True)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b in range(B):
+        qq, kk, vv = _oracle_block(q[b].numpy().reshape(-1), k[b].numpy().reshape(-1),
+                                   v[b].numpy().reshape(-1), np.arange(S), None if wq is None
+                                   else wq.numpy(), None if wk is None else wk.numpy(), rope,
+                                   hd, H, Hkv, hd, eps)
+        # The stored cache holds bf16 post-RoPE K (the GPU's operand).
+        kc = cache_k[b].float().cpu().numpy().reshape(-1)
+        np.testing.assert_allclose(kc, kk, atol=1e-2, rtol=1e-2)
+        ref = oracle_attention(qq, kk, vv, nq=S, nk=S, h=H, hkv=Hkv, hd=hd, scale=hd ** -0.5)
+        check_close(got[b], ref, H, hd, what=f"block qk_norm={qk_norm} b={b}")
+
+
+def test_block_with_cache_reuse_over_steps():
+    # c4-shaped (scaled down): 32 active canvas rows in the middle of the
+    # sequence attend to cached prefix/suffix K/V plus themselves; the cache is
+    # reused over several steps with fresh active rows each step.
+    B, n_total, na, H, Hkv, hd = 2, 600, 32, 8, 2, 128
+    start = 280
+    active = np.arange(start, start + na)
+    cached = np.concatenate([np.arange(0, start), np.arange(start + na, n_total)])
+    rope = ca.build_rope_cache(4096, hd, 5e5)
+    rope_d = torch.from_numpy(rope).cuda()
+    g = torch.Generator().manual_seed(41)
+    cache_k = bf16_round(randn(g, B, n_total, Hkv, hd)).to(torch.bfloat16).cuda()
+    cache_v = bf16_round(randn(g, B, n_total, Hkv, hd)).to(torch.bfloat16).cuda()
+    pos = torch.from_numpy(np.tile(active, (B, 1)).astype(np.int32)).cuda()
+    q_work = torch.empty(B, na, H, hd, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(B, na, H, hd, device="cuda")
+    for step in range(3):
+        before_k = cache_k.float().cpu().numpy()
+        before_v = cache_v.float().cpu().numpy()
+        q = bf16_round(randn(g, B, na, H, hd))
+        k = bf16_round(randn(g, B, na, Hkv, hd))
+        v = bf16_round(randn(g, B, na, Hkv, hd))
+        ca.attention_block_dev(q.to(torch.bfloat16).cuda(), k.to(torch.bfloat16).cuda(),
+                               v.to(torch.bfloat16).cuda(), batch=B, n_active=na,
+                               active_pos=pos, rope=rope_d, rope_len=4096, rope_dim=hd,
+                               cache_k=cache_k, cache_v=cache_v, n_total=n_total,
+                               q_work=q_work, out=out, n_head=H, n_head_kv=Hkv, head_dim=hd,
+                               out_f32=True, scale=hd ** -0.5, precise=True)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for b in range(B):
+            qq, kk, vv = _oracle_block(q[b].numpy().reshape(-1), k[b].numpy().reshape(-1),
+                                       v[b].numpy().reshape(-1), active, None, None, rope, hd,
+                                       H, Hkv, hd, 1e-6)
+            # Keys in the reference's order: [cached asc | active asc] (forward.rs:92-96).
+            kc, vc = orc.cache_gather(before_k[b].reshape(-1), before_v[b].reshape(-1),
+                                      Hkv * hd, cached)
+            kf = np.concatenate([kc, kk])
+            vf = np.concatenate([vc, vv])
+            ref = oracle_attention(qq, kf, vf, nq=na, nk=n_total, h=H, hkv=Hkv, hd=hd,
+                                   q_pos=active, k_pos=np.concatenate([cached, active]),
+                                   scale=hd ** -0.5)
+            check_close(got[b], ref, H, hd, what=f"cached step {step} b={b}")
+        # Cached rows are untouched; active rows now hold the new post-RoPE K/V.
+        after_k = cache_k.float().cpu().numpy()
+        np.testing.assert_array_equal(after_k[:, cached], before_k[:, cached])
