@@ -1,0 +1,588 @@
+#!/usr/bin/env python
+"""bench.py -- canvas-attention throughput on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3]
+                    [--impl ours|reference]
+
+A step is one pass of the attention hot path over one synthetic batch of the
+named config: for every layer of the config, the fused block entry point
+(QK RMSNorm -> RoPE -> K/V cache store -> attention, src/model/forward.rs:
+296-343) through the C ABI. Inputs are resident in HBM when timing starts.
+
+Configs (seeded N(0,1) bf16 inputs):
+  c1  B1  S128   H32/32  hd128  theta 5e5
+  c2  B4  S1024  H28/4   hd128  theta 1e6
+  c3  B8  S4096  H16/16  hd128  theta 5e4, QK RMSNorm (eps 1e-6, gains U(0.5,1.5))
+  c4  B16 32 active queries at positions 2048..2079 over a 4128-position
+      cache (4096 cached + 32 active), H32/8 hd128; the cache is reused and
+      each step brings fresh active Q/K/V
+  c5  B4  S8192  H16/8 hd256, 6 layers: 5 sliding (window 512, theta 1e4) +
+      1 global (theta 1e6), soft-cap 50 (extension), scale 1/16
+Default workload: c3, the 4k-token bidirectional case the north-star target
+names. Multi-GPU is weak scaling: every rank runs its own full batch of the
+config (sequences are independent, so no collective is on the data path).
+
+Metric: TFLOP/s = 4 * head_dim * visible (query, key) pairs * n_head summed
+over the batch and layers, divided by time (softmax, RoPE and norms excluded).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "diffuse-rs_b200"))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+
+CONFIGS = {
+    "c1": dict(B=1, na=128, n_total=128, start=0, H=32, Hkv=32, hd=128, qk_norm=False,
+               layers=[(None, 5e5)], softcap=0.0, scale=128 ** -0.5,
+               desc="LLaDA-8B single layer, B1 S128 H32/32 hd128"),
+    "c2": dict(B=4, na=1024, n_total=1024, start=0, H=28, Hkv=4, hd=128, qk_norm=False,
+               layers=[(None, 1e6)], softcap=0.0, scale=128 ** -0.5,
+               desc="Dream-7B GQA, B4 S1024 H28/4 hd128"),
+    "c3": dict(B=8, na=4096, n_total=4096, start=0, H=16, Hkv=16, hd=128, qk_norm=True,
+               layers=[(None, 5e4)], softcap=0.0, scale=128 ** -0.5,
+               desc="LLaDA-MoE + QK RMSNorm, B8 S4096 H16/16 hd128"),
+    "c4": dict(B=16, na=32, n_total=4128, start=2048, H=32, Hkv=8, hd=128, qk_norm=False,
+               layers=[(None, 5e5)], softcap=0.0, scale=128 ** -0.5,
+               desc="KV-cache block decode, B16 x 32 queries over 4128 keys, H32/8 hd128"),
+    "c5": dict(B=4, na=8192, n_total=8192, start=0, H=16, Hkv=8, hd=256, qk_norm=True,
+               layers=[(512, 1e4)] * 5 + [(None, 1e6)], softcap=50.0, scale=256 ** -0.5,
+               desc="DiffusionGemma hybrid, B4 S8192 H16/8 hd256, 5 sliding(512)+1 global"),
+}
+
+
+def visible_pairs(na, n_total, start, window):
+    """Visible (query, key) pairs of one sequence: queries at positions
+    start..start+na-1, keys at 0..n_total-1, visible iff |dq - dk| < window."""
+    if window is None:
+        return na * n_total
+    tot = 0
+    for qp in range(start, start + na):
+        lo = max(0, qp - window + 1)
+        hi = min(n_total - 1, qp + window - 1)
+        tot += hi - lo + 1
+    return tot
+
+
+def layer_flops(cfg, window):
+    return 4.0 * cfg["hd"] * cfg["H"] * cfg["B"] * visible_pairs(
+        cfg["na"], cfg["n_total"], cfg["start"], window)
+
+
+def step_flops(cfg):
+    return sum(layer_flops(cfg, w) for w, _ in cfg["layers"])
+
+
+def layer_bytes(cfg):
+    """Algorithmic HBM bytes of one attention launch: Q read once, K and V read
+    once per kv head (the whole cache for c4), O written once, all bf16."""
+    B, H, Hkv, hd = cfg["B"], cfg["H"], cfg["Hkv"], cfg["hd"]
+    return 2 * B * hd * (2 * cfg["na"] * H + 2 * cfg["n_total"] * Hkv)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm=d["hbm_gbs"], tflops=d["bf16_tflops"],
+                    tflops_sustained=d["bf16_tflops_sustained"], source="measured")
+    return dict(hbm=6650.0, tflops=1590.0, tflops_sustained=1400.0, source="fallback")
+
+
+def load_traffic(config):
+    """Per-launch DRAM bytes of the attention kernel from a committed ncu
+    summary (profiles/attn_fwd_dram_traffic.txt: '<config> <bytes>' lines)."""
+    p = os.path.join(ROOT, "profiles", "attn_fwd_dram_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) == 2 and parts[0] == config:
+                return float(parts[1])
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu_index), "-lms", "50"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.path is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+class Workload:
+    """Device tensors for one rank's batch of one config."""
+
+    def __init__(self, cfg, device, seed):
+        import torch
+        import canvas_attn as ca
+        self.ca, self.torch, self.cfg = ca, torch, cfg
+        B, na, nt, H, Hkv, hd = (cfg[k] for k in ("B", "na", "n_total", "H", "Hkv", "hd"))
+        g = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+
+        def rnd(*shape):
+            return torch.randn(*shape, generator=g, device=device, dtype=torch.float32).to(bf)
+
+        self.n_sets = 2  # fresh active Q/K/V alternate between steps
+        self.layers = []
+        for (window, theta) in cfg["layers"]:
+            rope = torch.from_numpy(ca.build_rope_cache(max(4096, nt), hd, theta)).to(device)
+            L = dict(window=window, rope=rope, rope_len=max(4096, nt),
+                     q=[rnd(B, na, H, hd) for _ in range(self.n_sets)],
+                     k=[rnd(B, na, Hkv, hd) for _ in range(self.n_sets)],
+                     v=[rnd(B, na, Hkv, hd) for _ in range(self.n_sets)],
+                     cache_k=rnd(B, nt, Hkv, hd), cache_v=rnd(B, nt, Hkv, hd),
+                     q_work=torch.empty(B, na, H, hd, dtype=bf, device=device),
+                     out=torch.empty(B, na, H, hd, dtype=bf, device=device))
+            if cfg["qk_norm"]:
+                L["wq"] = torch.rand(hd, generator=g, device=device) + 0.5
+                L["wk"] = torch.rand(hd, generator=g, device=device) + 0.5
+            self.layers.append(L)
+        pos = torch.arange(cfg["start"], cfg["start"] + na, dtype=torch.int32, device=device)
+        self.pos = pos.repeat(B, 1).contiguous()
+        self.stream = torch.cuda.current_stream(device)
+
+    def block_args(self, L, i):
+        c = self.cfg
+        return self.ca.make_block_args(
+            L["q"][i], L["k"][i], L["v"][i], batch=c["B"], n_active=c["na"],
+            active_pos=self.pos, rope=L["rope"], rope_len=L["rope_len"], rope_dim=c["hd"],
+            cache_k=L["cache_k"], cache_v=L["cache_v"], n_total=c["n_total"],
+            q_work=L["q_work"], out=L["out"], n_head=c["H"], n_head_kv=c["Hkv"],
+            head_dim=c["hd"], q_norm_w=L.get("wq"), k_norm_w=L.get("wk"), rms_eps=1e-6,
+            sliding_window=L["window"], scale=c["scale"], softcap=c["softcap"])
+
+    def step(self, i):
+        import ctypes
+        sp = self.stream.cuda_stream
+        for L in self.layers:
+            a = self.block_args(L, i % self.n_sets)
+            rc = self.ca.lib.ca_attention_block_dev(ctypes.byref(a), sp)
+            if rc != 0:
+                raise self.ca.CaError(rc, "ca_attention_block_dev")
+
+    launches_per_step = property(lambda self: 2 * len(self.layers))
+
+    def attn_args(self, L):
+        c = self.cfg
+        return self.ca.make_dev_args(
+            L["q_work"], L["cache_k"], L["cache_v"], L["out"], batch=c["B"], sq=c["na"],
+            sk=c["n_total"], n_head=c["H"], n_head_kv=c["Hkv"], head_dim=c["hd"],
+            q_pos=self.pos, sliding_window=L["window"], scale=c["scale"],
+            softcap=c["softcap"])
+
+    def attn_only(self, L):
+        import ctypes
+        a = self.attn_args(L)
+        rc = self.ca.lib.ca_attention_dev(ctypes.byref(a), self.stream.cuda_stream)
+        if rc != 0:
+            raise self.ca.CaError(rc, "ca_attention_dev")
+
+    def input_bytes(self):
+        return sum(t.numel() * t.element_size() for L in self.layers
+                   for t in (L["q"][0], L["k"][0], L["v"][0], L["cache_k"], L["cache_v"]))
+
+
+class CpuSample:
+    """A bounded sample of one config's (head, query) rows for the CPU
+    restatement of the reference's rayon/AVX2 attention (oracle/, the
+    reference's own Rust cannot be built here). Rows are exact: each row's
+    output is independent of the others, so a subset times the same code."""
+
+    def __init__(self, cfg, seed=0):
+        import numpy as np
+        from oracle import oracle as orc
+        self.np, self.orc, self.cfg = np, orc, cfg
+        rng = np.random.default_rng(seed)
+        c = cfg
+        nk = c["n_total"]
+
+        def rnd(n):
+            return rng.standard_normal(n, dtype=np.float32)
+
+        self.q = rnd(c["na"] * c["H"] * c["hd"])
+        self.k = rnd(nk * c["Hkv"] * c["hd"])
+        self.v = rnd(nk * c["Hkv"] * c["hd"])
+        self.q_pos = np.arange(c["start"], c["start"] + c["na"], dtype=np.int64)
+        self.k_pos = np.arange(nk, dtype=np.int64)
+        self.threads = orc.max_threads()
+        self.kind = orc.ROW_AVX2 if orc.have_avx2() else orc.ROW_SCALAR
+        self.out = np.zeros(c["na"] * c["H"] * c["hd"], dtype=np.float32)
+
+    def row_visible(self, qpos, window):
+        if window is None:
+            return self.cfg["n_total"]
+        return min(self.cfg["n_total"] - 1, qpos + window - 1) - max(0, qpos - window + 1) + 1
+
+    def run(self, n_rows):
+        """Runs about n_rows rows spread over every layer; returns (flops, seconds)."""
+        np, c = self.np, self.cfg
+        n_tasks = c["H"] * c["na"]
+        per_layer = max(1, n_rows // len(c["layers"]))
+        flops, secs = 0.0, 0.0
+        for window, _theta in c["layers"]:
+            tasks = np.unique(np.linspace(0, n_tasks - 1, min(per_layer, n_tasks)).astype(np.int64))
+            qrows = tasks % c["na"]
+            flops += 4.0 * c["hd"] * sum(self.row_visible(int(self.q_pos[r]), window)
+                                         for r in qrows)
+            t0 = time.perf_counter()
+            self.orc.attention(self.q, self.k, self.v, nq=c["na"], nk=c["n_total"],
+                               n_head=c["H"], n_head_kv=c["Hkv"], head_dim=c["hd"],
+                               q_pos=self.q_pos, k_pos=self.k_pos, sliding_window=window,
+                               scale=c["scale"], softcap=c["softcap"], kind=self.kind,
+                               threads=self.threads, tasks=tasks, out=self.out)
+            secs += time.perf_counter() - t0
+        return flops, secs
+
+    def calibrate(self, target_s):
+        n = 64 * len(self.cfg["layers"])
+        self.run(n)  # thread-pool start-up
+        f, s = self.run(4 * n)
+        return max(16, int(4 * n / max(s, 1e-6) * target_s))
+
+    def describe(self, n_rows, config):
+        return (f"{n_rows} (head, query) rows of one {config} sequence spread over "
+                f"{len(self.cfg['layers'])} layer(s), {self.cfg['n_total']} keys each")
+
+
+class E2E:
+    """The reference-facing call with HOST buffers: ca_attention_host_f32,
+    i.e. attention(out, q, k, v, s, qr, kr) (src/model/attention.rs:106) on
+    pinned fp32 host arrays, once per sequence and layer as the reference calls
+    it. Host->device copies of Q/K/V and the device->host copy of out happen
+    inside each call."""
+
+    def __init__(self, cfg, seed=0):
+        import numpy as np
+        import torch
+        import canvas_attn as ca
+        self.ca, self.cfg = ca, cfg
+        c = cfg
+        g = torch.Generator().manual_seed(seed)
+
+        def pinned(n):
+            t = torch.randn(n, generator=g, dtype=torch.float32).pin_memory()
+            return t, t.numpy()
+
+        nk = c["n_total"]
+        self._keep = []
+        for name, n in (("q", c["na"] * c["H"] * c["hd"]), ("k", nk * c["Hkv"] * c["hd"]),
+                        ("v", nk * c["Hkv"] * c["hd"]), ("out", c["na"] * c["H"] * c["hd"])):
+            t, a = pinned(n)
+            self._keep.append(t)
+            setattr(self, name, a)
+        # Key rows in the reference's cached order [cached asc | active asc]
+        # (src/model/forward.rs:92-96); without a cache, keys = queries' positions.
+        act = np.arange(c["start"], c["start"] + c["na"])
+        if nk > c["na"]:
+            cached = np.setdiff1d(np.arange(nk), act)
+            self.k_pos = np.concatenate([cached, act])
+        else:
+            self.k_pos = act
+        self.q_pos = act
+        self.calls = len(c["layers"]) * c["B"]
+        self.h2d = self.calls * 4 * (self.q.size + self.k.size + self.v.size)
+        self.d2h = self.calls * 4 * self.out.size
+
+    def step(self):
+        c = self.cfg
+        for window, _theta in c["layers"]:
+            s = self.ca.AttnShape(c["na"], c["n_total"], c["H"], c["Hkv"], c["hd"], window,
+                                  None, c["scale"], c["softcap"])
+            qr, kr = self.ca.Rows(self.q_pos), self.ca.Rows(self.k_pos)
+            for _b in range(c["B"]):
+                self.ca.attention(self.out, self.q, self.k, self.v, s, qr, kr)
+
+
+def dist_setup(want_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    if want_gpus != world and rank == 0:
+        print(f"note: --gpus {want_gpus} but WORLD_SIZE {world}; using {world}", file=sys.stderr)
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def physical_gpu_index(local):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+def run_ours(args, cfg):
+    import torch
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    wl = Workload(cfg, dev, seed=1234 + rank)
+    ws = wl.input_bytes()
+    flush = ws < 2 * L2_BYTES
+    scratch = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
+
+    for i in range(args.warmup):
+        wl.step(i)
+    torch.cuda.synchronize()
+    assert wl.ca.device_status(wl.stream.cuda_stream) == 0, "device-side timeout in warm-up"
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(physical_gpu_index(local)) as clk:
+        for i in range(args.steps):
+            if flush:
+                scratch.zero_()
+            starts[i].record(wl.stream)
+            wl.step(i)
+            ends[i].record(wl.stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    ms_total = max_over_ranks(ms_local, world)
+    status = wl.ca.device_status(wl.stream.cuda_stream)
+    assert status == 0, f"device-side status {status}"
+    clocks = clk.summary()
+
+    flops = step_flops(cfg)
+    value = world * flops * args.steps / (ms_total * 1e-3) / 1e12
+
+    # Dominant kernel: the attention kernel alone, on the same prepared tensors.
+    reps = max(3, min(args.steps, 50))
+    attn_ms = 0.0
+    for L in wl.layers:
+        wl.attn_only(L)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(reps)]
+        torch.cuda.synchronize()
+        for a, b in ev:
+            if flush:
+                scratch.zero_()
+            a.record(wl.stream)
+            wl.attn_only(L)
+            b.record(wl.stream)
+        torch.cuda.synchronize()
+        attn_ms += sum(a.elapsed_time(b) for a, b in ev) / reps
+    peaks = load_peaks()
+    hbm_bound = args.config == "c4"
+    if hbm_bound:
+        per_launch = sum(layer_bytes(cfg) for _ in cfg["layers"])
+        achieved = per_launch / (attn_ms * 1e-3) / 1e9
+        roof = dict(bound="hbm", achieved=round(achieved, 1), peak=peaks["hbm"], unit="GB/s")
+    else:
+        achieved = flops / (attn_ms * 1e-3) / 1e12
+        roof = dict(bound="tensor", achieved=round(achieved, 1), peak=peaks["tflops"],
+                    unit="TFLOP/s")
+    roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
+    roof["peak_source"] = peaks["source"] + (" burst" if not hbm_bound else " copy")
+    roof["traffic"] = load_traffic(args.config)
+    roof["kernel_ms"] = round(attn_ms, 4)
+
+    # End to end through the host-buffer drop-in entry point.
+    e2e = None
+    if not args.no_e2e:
+        ee = E2E(cfg)
+        ee.step()
+        torch.cuda.synchronize()
+        n_e2e = max(1, min(args.steps, args.e2e_steps))
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            ee.step()
+        dt = max_over_ranks(time.perf_counter() - t0, world)
+        e2e = dict(value=round(world * flops * n_e2e / dt / 1e12, 3), unit="TFLOP/s",
+                   h2d_bytes_per_step=ee.h2d, d2h_bytes_per_step=ee.d2h, steps=n_e2e,
+                   api="ca_attention_host_f32 (fp32 host buffers, precise weights)")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cs = CpuSample(cfg)
+        n_rows = cs.calibrate(args.cpu_seconds)
+        f, s = cs.run(n_rows)
+        cpu = dict(value=f / s / 1e12, unit="TFLOP/s", cores=cs.threads, kind="port",
+                   sample=cs.describe(n_rows, args.config) + f", {s:.1f} s")
+
+    if rank == 0:
+        line = {
+            "metric": "canvas-attention TFLOP/s",
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_total / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1), bf16)",
+            "config": {"workload": args.config, "desc": cfg["desc"],
+                       "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * world,
+                       "seq_q": cfg["na"], "seq_k": cfg["n_total"],
+                       "layers": len(cfg["layers"]),
+                       "tokens_per_s": round(world * cfg["B"] * cfg["na"] * args.steps
+                                             / (ms_total * 1e-3), 1),
+                       "l2": "flushed between steps (working set < 2x L2)" if flush
+                       else "inputs larger than L2, no flush",
+                       "parallelism": f"dp{world} (independent sequences per rank)"},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": wl.launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args, cfg):
+    """The reference's CPU implementation of the path (restated in C under
+    oracle/, all host threads) on a bounded sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    cs = CpuSample(cfg)
+    n_rows = cs.calibrate(args.ref_step_seconds)
+    for _ in range(args.warmup):
+        cs.run(max(16, n_rows // 8))
+    tf, ts = 0.0, 0.0
+    for _ in range(args.steps):
+        f, s = cs.run(n_rows)
+        tf += f
+        ts += s
+    value = tf / ts / 1e12
+    sample = cs.describe(n_rows, args.config) + " per step"
+    line = {
+        "impl": "reference",
+        "metric": "canvas-attention TFLOP/s",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ts / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": args.config, "desc": cfg["desc"]},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cs.threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[1])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=2.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

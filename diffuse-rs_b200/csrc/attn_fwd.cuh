@@ -7,12 +7,15 @@
 // (src/model/attention.rs:35-57, :106-186): per query row, softmax over every
 // visible key of scale * q.k, times V; rows with no visible key give NaN.
 //
-// Warp roles (256 threads):
-//   warp 0      TMA producer: Q once, then K/V tiles through an ST-stage ring
+// Warp roles (384 threads):
+//   warp 0      TMA producer: Q once, then K tiles through an ST-stage ring
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one elected lane)
 //   warps 2-3   prologue: build the list of key tiles that have any visible
-//               (query, key) pair, flagging tiles that need per-element masks
-//   warps 4-7   softmax + O correction + epilogue; thread r owns TMEM lane r
+//               (query, key) pair, flagging tiles that need per-element masks;
+//               afterwards warp 3 streams V tiles through their own ring
+//   warps 4-11  softmax + O correction + epilogue; TMEM lane r (= row r) is
+//               shared by warps 4 + r/32 and 8 + r/32, each owning half of the
+//               tile's key columns and half of O's columns
 //
 // Pipeline per visible key tile j (S double-buffered in TMEM, P in smem):
 //   S[j&1] = Q K_j^T           (tcgen05.mma, SS, fp32 accumulate in TMEM)
@@ -32,6 +35,7 @@
 namespace ca {
 
 constexpr int kNoWindow = INT_MAX;
+constexpr int kFwdThreads = 384;  // 4 control warps + 8 softmax warps
 
 struct FwdParams {
   void* out;
@@ -60,7 +64,7 @@ template <int HDP_, int BN_, int ST_, bool PRECISE_ = false>
 struct FwdCfg {
   static constexpr int HDP = HDP_;  // head_dim padded to a multiple of 64
   static constexpr int BN = BN_;    // keys per tile
-  static constexpr int ST = ST_;    // K/V pipeline stages
+  static constexpr int ST = ST_;    // stages of each of the K and V rings
   // PRECISE: P is split into bf16 hi + lo terms (two PV MMAs), so the softmax
   // weights reach the tensor core with ~16 significant bits instead of 8.
   static constexpr bool PRECISE = PRECISE_;
@@ -78,23 +82,27 @@ struct FwdCfg {
   static constexpr int kOffV = kOffK + ST * kKVBytes;
   static constexpr int kOffP = kOffV + ST * kKVBytes;
   static constexpr int kOffBar = kOffP + kPBytes;
-  // Barriers: Qfull, Kfull[ST], Vfull[ST], KVempty[ST], Sfull[2], Pfull, Oready, Fin
+  // Barriers. K and V stages are released separately: a K stage as soon as
+  // its Q K^T MMA completes, a V stage when its P V MMA completes, so the
+  // next key tile's load overlaps the current tile's softmax.
   static constexpr int kBarQ = 0;
-  static constexpr int kBarK = 1;
-  static constexpr int kBarV = 1 + ST;
-  static constexpr int kBarE = 1 + 2 * ST;
-  static constexpr int kBarS = 1 + 3 * ST;
-  static constexpr int kBarP = kBarS + 2;
-  static constexpr int kBarO = kBarP + 1;
-  static constexpr int kBarF = kBarO + 1;
-  static constexpr int kNumBars = kBarF + 1;
+  static constexpr int kBarK = 1;             // [ST] K tile landed
+  static constexpr int kBarV = kBarK + ST;    // [ST] V tile landed
+  static constexpr int kBarKE = kBarV + ST;   // [ST] K stage free
+  static constexpr int kBarVE = kBarKE + ST;  // [ST] V stage free
+  static constexpr int kBarS = kBarVE + ST;   // [2] S buffer holds Q K^T
+  static constexpr int kBarP = kBarS + 2;     // P written (8 softmax warps)
+  static constexpr int kBarO = kBarP + 1;     // P V of the latest tile done
+  static constexpr int kBarF = kBarO + 1;     // all MMAs done
+  static constexpr int kBarX = kBarF + 1;     // [4] softmax warp-pair exchange
+  static constexpr int kNumBars = kBarX + 4;
   // Largest key-tile count per sequence (keys <= kMaxTiles * BN).
-  static constexpr int kMaxTiles = (PRECISE && HDP == 256) ? 512 : 1024;
+  static constexpr int kMaxTiles = (PRECISE && HDP == 256) ? 256 : 1024;
   static constexpr int kOffList = kOffBar + kNumBars * 8;
-  static constexpr int kOffFlags = kOffList + kMaxTiles * 2;
-  static constexpr int kOffMisc = kOffFlags + kMaxTiles;
+  static constexpr int kOffXch = kOffList + kMaxTiles * 2;  // float [parity][half][128]
+  static constexpr int kOffMisc = kOffXch + 2 * 2 * 128 * 4;
   static constexpr int kMiscBytes = 64;
-  static constexpr int kSmemBytes = kOffMisc + kMiscBytes + 1024;  // + base alignment slack
+  static constexpr int kSmemBytes = kOffMisc + kMiscBytes;
   static constexpr int kTmemCols = 512;
   static constexpr int kOCol = 2 * BN;  // O accumulator columns [2BN, 2BN + HDP)
   static constexpr uint32_t kIdescS = umma_idesc_bf16(128, BN, 0, 0);
@@ -153,11 +161,12 @@ __device__ __forceinline__ void seq_range(const FwdParams& p, int b, int& q_beg,
 // Prologue of warps 2-3: classify every key tile of the sequence against this
 // CTA's query tile (0 = no visible pair, 1 = every pair visible, 2 = needs
 // per-element masks) and compact the visible ones into `list` (bit 15 marks
-// partial tiles). Returns nothing; writes *n_tiles.
+// partial tiles). The per-tile flags are first written in place into `list`
+// and then compacted; misc[1] receives the count.
 template <class C>
 __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_beg, int k_len,
-                                int qtile, uint16_t* list, uint8_t* flags, int* misc,
-                                int tid64) {
+                                int qtile, uint16_t* list, int* misc, int tid64) {
+  uint16_t* flags = list;
   const int lane = tid64 & 31;
   const int w = tid64 >> 5;  // 0..1
   const int n_kt = (k_len + C::BN - 1) / C::BN;
@@ -206,7 +215,7 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
       ksmin = __reduce_min_sync(0xffffffffu, ksmin);
       ksmax = __reduce_max_sync(0xffffffffu, ksmax);
       if (lane == 0) {
-        uint8_t f = 2;
+        uint16_t f = 2;
         const bool ragged = (kt + 1) * C::BN > k_len;
         if (nt <= 0 || qsmax < ksmin || ksmax < qsmin) {
           f = 0;
@@ -230,8 +239,8 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
     int count = 0;
     for (int base = 0; base < n_kt; base += 32) {
       const int kt = base + lane;
-      const uint8_t f = kt < n_kt ? flags[kt] : 0;
-      const unsigned ball = __ballot_sync(0xffffffffu, f != 0);
+      const uint16_t f = kt < n_kt ? flags[kt] : 0;
+      const unsigned ball = __ballot_sync(0xffffffffu, f != 0);  // all reads precede writes
       if (f) {
         const int pos = count + __popc(ball & ((1u << lane) - 1u));
         list[pos] = static_cast<uint16_t>(kt | (f == 2 ? 0x8000 : 0));
@@ -247,14 +256,19 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
 namespace ca {
 
 template <class C>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
+  // static shared memory, so the dynamic window starts 1024-aligned; if it
+  // ever did not, report it instead of computing garbage.
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicExch(&g_device_error, kErrLayout);
+    return;
+  }
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -273,7 +287,6 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t bar0 = smem_u32(smem + C::kOffBar);
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * i; };
   uint16_t* list = reinterpret_cast<uint16_t*>(smem + C::kOffList);
-  uint8_t* flags = smem + C::kOffFlags;
   int* misc = reinterpret_cast<int*>(smem + C::kOffMisc);  // [0]=tmem base [1]=n_tiles
 
   if (tid == 0) {
@@ -281,13 +294,15 @@ __global__ void __launch_bounds__(256, 1)
     for (int s = 0; s < ST; ++s) {
       mbar_init(bar(C::kBarK + s), 1);
       mbar_init(bar(C::kBarV + s), 1);
-      mbar_init(bar(C::kBarE + s), 1);
+      mbar_init(bar(C::kBarKE + s), 1);
+      mbar_init(bar(C::kBarVE + s), 1);
     }
     mbar_init(bar(C::kBarS), 1);
     mbar_init(bar(C::kBarS + 1), 1);
-    mbar_init(bar(C::kBarP), 4);
+    mbar_init(bar(C::kBarP), 8);
     mbar_init(bar(C::kBarO), 1);
     mbar_init(bar(C::kBarF), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(bar(C::kBarX + i), 2);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -301,7 +316,7 @@ __global__ void __launch_bounds__(256, 1)
     tmem_relinquish();
   }
   if (warp == 2 || warp == 3) {
-    build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, qtile, list, flags, misc, tid - 64);
+    build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, qtile, list, misc, tid - 64);
   }
   tc_fence_before();
   __syncthreads();
@@ -310,36 +325,37 @@ __global__ void __launch_bounds__(256, 1)
   const int n = misc[1];
   bool dead = false;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == 3) {
+    // ------------------------------------------------------------ producers
+    // Warp 0 streams Q and the K tiles, warp 3 the V tiles: the two rings
+    // drain at different times (K after Q K^T, V after P V).
     if (lane == 0) {
-      const int q_tok0 = q_beg + qtile * p.QT;
-      mbar_arrive_expect_tx(bar(C::kBarQ), C::kChunks * 128u * p.R);
+      const bool is_k = warp == 0;
+      const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
+      const uint32_t ring = is_k ? sK : sV;
+      const int full = is_k ? C::kBarK : C::kBarV;
+      const int empty = is_k ? C::kBarKE : C::kBarVE;
+      if (is_k) {
+        const int q_tok0 = q_beg + qtile * p.QT;
+        mbar_arrive_expect_tx(bar(C::kBarQ), C::kChunks * 128u * p.R);
 #pragma unroll
-      for (int c = 0; c < C::kChunks; ++c)
-        tma_load_3d(sQ + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64, kvh * p.G, q_tok0);
-      for (int j = 0; j < n && !dead; ++j) {
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(sQ + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64, kvh * p.G, q_tok0);
+      }
+      for (int j = 0; j < n; ++j) {
         const int s = j % ST;
-        if (j >= ST && !mbar_wait(bar(C::kBarE + s), ((j / ST) - 1) & 1, dead)) break;
+        if (j >= ST && !mbar_wait(bar(empty + s), ((j / ST) - 1) & 1, dead)) break;
         const int krow = k_beg + (list[j] & 0x7fff) * BN;
-        mbar_arrive_expect_tx(bar(C::kBarK + s), C::kKVBytes);
+        mbar_arrive_expect_tx(bar(full + s), C::kKVBytes);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sK + s * C::kKVBytes + c * C::kKChunk, &tm_k, bar(C::kBarK + s), c * 64,
-                      kvh, krow);
-        mbar_arrive_expect_tx(bar(C::kBarV + s), C::kKVBytes);
-#pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sV + s * C::kKVBytes + c * C::kKChunk, &tm_v, bar(C::kBarV + s), c * 64,
-                      kvh, krow);
+          tma_load_3d(ring + s * C::kKVBytes + c * C::kKChunk, tm, bar(full + s), c * 64, kvh,
+                      krow);
       }
       // Leave no bulk copy in flight: wait (bounded) for the last loads.
       bool d2 = false;
-      mbar_wait(bar(C::kBarQ), 0, d2);
-      for (int j = max(0, n - ST); j < n; ++j) {
-        mbar_wait(bar(C::kBarK + j % ST), (j / ST) & 1, d2);
-        mbar_wait(bar(C::kBarV + j % ST), (j / ST) & 1, d2);
-      }
+      if (is_k) mbar_wait(bar(C::kBarQ), 0, d2);
+      for (int j = max(0, n - ST); j < n; ++j) mbar_wait(bar(full + j % ST), (j / ST) & 1, d2);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -361,7 +377,7 @@ __global__ void __launch_bounds__(256, 1)
           }
         }
         umma_commit(bar(C::kBarO));
-        umma_commit(bar(C::kBarE + s));
+        umma_commit(bar(C::kBarVE + s));
         return true;
       };
       if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead)) {
@@ -378,6 +394,7 @@ __global__ void __launch_bounds__(256, 1)
             umma_ss(sdst, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
           }
           umma_commit(bar(C::kBarS + (j & 1)));
+          umma_commit(bar(C::kBarKE + s));
           if (j >= 1 && !issue_pv(j - 1)) break;
         }
         if (!dead) issue_pv(n - 1);
@@ -389,9 +406,18 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax
-    const int wq = warp - 4;
+    // Warps w and w+4 share TMEM lane quarter wq (rows 32wq..32wq+31); `half`
+    // picks which half of each tile's key columns (and of O's columns) the
+    // warp owns. Row maxima and sums are combined through shared memory.
+    constexpr int BH = BN / 2;   // S columns per warp
+    constexpr int OH = HDP / 2;  // O columns per warp
+    const int sw = warp - 4;
+    const int wq = sw & 3;
+    const int half = sw >> 2;
     const int r = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    float* xch = reinterpret_cast<float*>(smem + C::kOffXch);  // [parity][half][128]
+    const uint32_t xbar = bar(C::kBarX + wq);
     const int t_local = qtile * p.QT + r / p.G;
     const bool row_valid = r < p.R && t_local < q_len;
     const int gq = q_beg + (row_valid ? t_local : 0);
@@ -413,47 +439,62 @@ __global__ void __launch_bounds__(256, 1)
       dead = __any_sync(0xffffffffu, dead);
       if (dead) break;
       tc_fence_after();
-      uint32_t sr[BN];
+      uint32_t sr[BH];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-        tmem_ld32(tmem + lane_off + (j & 1) * BN + c * 32,
+      for (int c = 0; c < BH / 32; ++c)
+        tmem_ld32(tmem + lane_off + (j & 1) * BN + half * BH + c * 32,
                   *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       tmem_wait_ld();
 
-      float mcand;
+      // Partial row max over this warp's columns (8 independent chains: one
+      // warp per SM sub-partition cannot hide a long dependent chain).
+      float pmax;
       const bool fast = fast_ok && !partial;
-      if (fast) {
-        float mx = u2f(sr[0]);
+      {
+        float mx8[8];
 #pragma unroll
-        for (int i = 1; i < BN; ++i) mx = fmaxf(mx, u2f(sr[i]));
-        mcand = mx * sl2;
-      } else {
-        float mx = -INFINITY;
+        for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
+        if (fast) {
 #pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          float t;
-          if (p.softcap != 0.f) {
-            const float x = u2f(sr[i]) * p.scale;
-            t = p.softcap * tanh_via_exp2(x / p.softcap) * 1.4426950408889634f;
-          } else {
-            t = u2f(sr[i]) * sl2;
-          }
-          if (partial) {
-            const int kl = kt * BN + i;
-            bool ok = kl < k_len;
-            if (ok && p.any_mask) {
-              const int g = k_beg + kl;
-              const int kp = p.k_pos ? p.k_pos[g] : kl;
-              const int ks = p.k_seq ? p.k_seq[g] : 0;
-              ok = visible_dev(qpos, kp, qseq, ks, p.window, qpre);
+          for (int i = 0; i < BH; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], u2f(sr[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < BH; ++i) {
+            float t;
+            if (p.softcap != 0.f) {
+              const float x = u2f(sr[i]) * p.scale;
+              t = p.softcap * tanh_via_exp2(x / p.softcap) * 1.4426950408889634f;
+            } else {
+              t = u2f(sr[i]) * sl2;
             }
-            if (!ok) t = -INFINITY;
+            if (partial) {
+              const int kl = kt * BN + half * BH + i;
+              bool ok = kl < k_len;
+              if (ok && p.any_mask) {
+                const int g = k_beg + kl;
+                const int kp = p.k_pos ? p.k_pos[g] : kl;
+                const int ks = p.k_seq ? p.k_seq[g] : 0;
+                ok = visible_dev(qpos, kp, qseq, ks, p.window, qpre);
+              }
+              if (!ok) t = -INFINITY;
+            }
+            sr[i] = f2u(t);
+            mx8[i & 7] = fmaxf(mx8[i & 7], t);
           }
-          sr[i] = f2u(t);
-          mx = fmaxf(mx, t);
         }
-        mcand = mx;
+        pmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                     fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       }
+      // Exchange with the partner warp (same rows, other columns).
+      xch[((j & 1) * 2 + half) * 128 + r] = pmax;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xbar);
+      mbar_wait(xbar, j & 1, dead);
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      const float rmax = fmaxf(pmax, xch[((j & 1) * 2 + (half ^ 1)) * 128 + r]);
+      const float mcand = fast ? rmax * sl2 : rmax;
+
       const bool resc = mcand > m + 8.f;
       float corr = 1.f;
       if (resc) {
@@ -461,11 +502,11 @@ __global__ void __launch_bounds__(256, 1)
         m = mcand;
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
-      float sum = 0.f;
-      uint32_t pk[BN / 2];
-      uint32_t pl[C::PRECISE ? BN / 2 : 1];
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[BH / 2];
+      uint32_t pl[C::PRECISE ? BH / 2 : 1];
 #pragma unroll
-      for (int i = 0; i < BN; i += 2) {
+      for (int i = 0; i < BH; i += 2) {
         float p0, p1;
         if (fast) {
           p0 = ex2_approx(fmaf(u2f(sr[i]), sl2, -mu));
@@ -474,7 +515,7 @@ __global__ void __launch_bounds__(256, 1)
           p0 = ex2_approx(u2f(sr[i]) - mu);
           p1 = ex2_approx(u2f(sr[i + 1]) - mu);
         }
-        sum += p0 + p1;
+        sum4[(i >> 1) & 3] += p0 + p1;
         pk[i / 2] = pack_bf16(p0, p1);
         if constexpr (C::PRECISE) {
           const float h0 = __uint_as_float(pk[i / 2] << 16);
@@ -482,9 +523,9 @@ __global__ void __launch_bounds__(256, 1)
           pl[i / 2] = pack_bf16(p0 - h0, p1 - h1);
         }
       }
-      l = l * corr + sum;
+      l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
 
-      // P's buffer and O are free once PV of the previous tile completed.
+      // P's buffer and O are free once P V of the previous tile completed.
       if (j > 0) {
         mbar_wait(bar(C::kBarO), (j - 1) & 1, dead);
         dead = __any_sync(0xffffffffu, dead);
@@ -492,9 +533,9 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-          for (int c = 0; c < HDP / 32; ++c) {
+          for (int c = 0; c < OH / 32; ++c) {
             uint32_t o[32];
-            const uint32_t ta = tmem + lane_off + C::kOCol + c * 32;
+            const uint32_t ta = tmem + lane_off + C::kOCol + half * OH + c * 32;
             tmem_ld32(ta, o);
             tmem_wait_ld();
 #pragma unroll
@@ -504,17 +545,16 @@ __global__ void __launch_bounds__(256, 1)
           tmem_wait_st();
         }
       }
-      // P row r: 128-byte rows, 16-byte units XOR-swizzled by (r & 7).
+      // P row r: 128-byte rows of 64 keys, 16-byte units XOR-swizzled by (r & 7).
 #pragma unroll
-      for (int cc = 0; cc < BN / 64; ++cc) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t addr = sP + cc * C::kPChunk + r * 128 + ((u ^ (r & 7)) << 4);
-          const int w0 = cc * 32 + u * 4;
-          st_shared_v4(addr, pk[w0], pk[w0 + 1], pk[w0 + 2], pk[w0 + 3]);
-          if constexpr (C::PRECISE)
-            st_shared_v4(addr + C::kPTermBytes, pl[w0], pl[w0 + 1], pl[w0 + 2], pl[w0 + 3]);
-        }
+      for (int u = 0; u < BH / 8; ++u) {
+        const int key0 = half * BH + u * 8;
+        const uint32_t addr =
+            sP + (key0 >> 6) * C::kPChunk + r * 128 + ((((key0 & 63) >> 3) ^ (r & 7)) << 4);
+        st_shared_v4(addr, pk[u * 4], pk[u * 4 + 1], pk[u * 4 + 2], pk[u * 4 + 3]);
+        if constexpr (C::PRECISE)
+          st_shared_v4(addr + C::kPTermBytes, pl[u * 4], pl[u * 4 + 1], pl[u * 4 + 2],
+                       pl[u * 4 + 3]);
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -530,13 +570,22 @@ __global__ void __launch_bounds__(256, 1)
       have_o = !dead;
       tc_fence_after();
     }
+    if (have_o) {  // row sum = both halves' partial sums (same running max)
+      xch[((n & 1) * 2 + half) * 128 + r] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xbar);
+      mbar_wait(xbar, n & 1, dead);
+      dead = __any_sync(0xffffffffu, dead);
+      have_o = !dead;
+      l += xch[((n & 1) * 2 + (half ^ 1)) * 128 + r];
+    }
     const float inv = have_o ? 1.f / l : __int_as_float(0x7fc00000);
     const int head = kvh * p.G + (r % p.G);
 #pragma unroll 1
-    for (int c = 0; c < HDP / 32; ++c) {
+    for (int c = 0; c < OH / 32; ++c) {
       uint32_t o[32];
       if (have_o) {
-        tmem_ld32(tmem + lane_off + C::kOCol + c * 32, o);
+        tmem_ld32(tmem + lane_off + C::kOCol + half * OH + c * 32, o);
         tmem_wait_ld();
       } else {
 #pragma unroll
@@ -547,7 +596,7 @@ __global__ void __launch_bounds__(256, 1)
                               static_cast<int64_t>(head) * p.hd;
 #pragma unroll
         for (int g8 = 0; g8 < 4; ++g8) {
-          const int col = c * 32 + g8 * 8;
+          const int col = half * OH + c * 32 + g8 * 8;
           if (col < p.hd) {
             float v[8];
 #pragma unroll

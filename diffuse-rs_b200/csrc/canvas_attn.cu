@@ -91,7 +91,7 @@ struct Launch {
     }
     const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
     dim3 grid(n_qtiles, p->n_head_kv, p->batch);
-    attn_fwd_kernel<C><<<grid, 256, C::kSmemBytes, st>>>(tq, tk, tv, *p);
+    attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, *p);
     return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
   }
 };
@@ -222,8 +222,19 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   pp.Hkv = Hkv;
   pp.hd = hd;
   const long long jobs = static_cast<long long>(a->batch) * a->n_active * (H + 2 * Hkv);
-  const int blocks = static_cast<int>(std::min<long long>((jobs + 7) / 8, 148LL * 16));
-  prep_block_kernel<<<blocks, 256, 8 * hd * sizeof(float), st>>>(pp);
+  const bool vec = aligned16(a->q) && aligned16(a->k) && aligned16(a->v) &&
+                   aligned16(a->q_work) && aligned16(a->cache_k) && aligned16(a->cache_v);
+  if (vec && (hd == 64 || hd == 128 || hd == 256)) {
+    const int rows_per_block = 8 * (32 / (hd / 8));
+    const int blocks = static_cast<int>(
+        std::min<long long>((jobs + rows_per_block - 1) / rows_per_block, 148LL * 32));
+    if (hd == 64) prep_block_vec_kernel<8><<<blocks, 256, 0, st>>>(pp);
+    else if (hd == 128) prep_block_vec_kernel<16><<<blocks, 256, 0, st>>>(pp);
+    else prep_block_vec_kernel<32><<<blocks, 256, 0, st>>>(pp);
+  } else {
+    const int blocks = static_cast<int>(std::min<long long>((jobs + 7) / 8, 148LL * 16));
+    prep_block_kernel<<<blocks, 256, 8 * hd * sizeof(float), st>>>(pp);
+  }
   if (cudaGetLastError() != cudaSuccess) return CA_ERR_CUDA;
 
   ca_dev_args d{};

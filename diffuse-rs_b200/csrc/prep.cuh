@@ -32,6 +32,11 @@ struct PrepParams {
   int batch, na, n_total, H, Hkv, hd;
 };
 
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // Sum of squares as the reference forms it: f32 products accumulated in f64.
 __device__ __forceinline__ float rms_scale(const float* x, int hd, int lane, float eps) {
   double ss = 0.0;
@@ -94,6 +99,108 @@ __global__ void __launch_bounds__(256) prep_block_kernel(const PrepParams p) {
     }
     for (int e = 2 * half + lane; e < p.hd; e += 32) dst[e] = __float2bfloat16_rn(buf[e]);
     __syncwarp();
+  }
+}
+
+// Vectorised form for head_dim in {64, 128, 256}: each lane owns 8
+// consecutive elements (one 16-byte load and store), a row spans LPR =
+// head_dim / 8 lanes and a warp handles 32 / LPR rows at once. The RoPE
+// partner element (i <-> i + rope_dim/2) is read back from a per-warp staging
+// row in shared memory.
+template <int LPR>
+__global__ void __launch_bounds__(256) prep_block_vec_kernel(const PrepParams p) {
+  constexpr int RPW = 32 / LPR;   // rows per warp
+  constexpr int HD = LPR * 8;
+  __shared__ float stage[8][RPW][HD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / LPR, sl = lane % LPR;
+  float* buf = stage[warp][sub];
+  const int per_tok = p.H + 2 * p.Hkv;
+  const long long jobs = static_cast<long long>(p.batch) * p.na * per_tok;
+  const long long wstride = static_cast<long long>(gridDim.x) * 8 * RPW;
+  for (long long base = (static_cast<long long>(blockIdx.x) * 8 + warp) * RPW; base < jobs;
+       base += wstride) {
+    const long long job = base + sub;
+    const bool active = job < jobs;
+    const long long jj = active ? job : base;
+    const long long tok = jj / per_tok;
+    const int r = static_cast<int>(jj % per_tok);
+    const int b = static_cast<int>(tok / p.na);
+    const int pos = p.pos[tok];
+    const __nv_bfloat16* src;
+    __nv_bfloat16* dst;
+    const float* w = nullptr;
+    bool norm = false, rope = true;
+    if (r < p.H) {
+      src = p.q + (tok * p.H + r) * HD;
+      dst = p.q_out + (tok * p.H + r) * HD;
+      w = p.q_norm_w;
+      norm = w != nullptr;
+    } else if (r < p.H + p.Hkv) {
+      const int h = r - p.H;
+      src = p.k + (tok * p.Hkv + h) * HD;
+      dst = p.cache_k + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
+      w = p.k_norm_w;
+      norm = w != nullptr;
+    } else {
+      const int h = r - p.H - p.Hkv;
+      src = p.v + (tok * p.Hkv + h) * HD;
+      dst = p.cache_v + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
+      norm = p.v_norm != 0;
+      rope = false;
+    }
+    const int e0 = sl * 8;
+    float x[8];
+    {
+      const uint4 raw = *reinterpret_cast<const uint4*>(src + e0);
+      const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        x[2 * i] = __uint_as_float(wv[i] << 16);
+        x[2 * i + 1] = __uint_as_float(wv[i] & 0xffff0000u);
+      }
+    }
+    // Every lane of the warp joins the reductions; `norm` may differ per row.
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += static_cast<double>(__fmul_rn(x[i], x[i]));
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (norm) {
+      const float sc =
+          __fdiv_rn(1.f, static_cast<float>(sqrt(ss / HD + static_cast<double>(p.eps))));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = w ? __fmul_rn(__fmul_rn(x[i], sc), w[e0 + i])
+                                           : __fmul_rn(x[i], sc);
+    }
+    const int half = rope ? p.rope_dim / 2 : 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) buf[e0 + i] = x[i];
+    __syncwarp();
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = e0 + i;
+      if (e < half) {
+        const float2 sc2 = reinterpret_cast<const float2*>(p.rope)[static_cast<long long>(pos) * half + e];
+        y[i] = __fsub_rn(__fmul_rn(x[i], sc2.y), __fmul_rn(buf[e + half], sc2.x));
+      } else if (e < 2 * half) {
+        const int j = e - half;
+        const float2 sc2 = reinterpret_cast<const float2*>(p.rope)[static_cast<long long>(pos) * half + j];
+        y[i] = __fadd_rn(__fmul_rn(buf[j], sc2.x), __fmul_rn(x[i], sc2.y));
+      } else {
+        y[i] = x[i];
+      }
+    }
+    __syncwarp();
+    if (active) {
+      uint4 o;
+      o.x = pack2_bf16(y[0], y[1]);
+      o.y = pack2_bf16(y[2], y[3]);
+      o.z = pack2_bf16(y[4], y[5]);
+      o.w = pack2_bf16(y[6], y[7]);
+      *reinterpret_cast<uint4*>(dst + e0) = o;
+    }
   }
 }
 

@@ -15,6 +15,8 @@ namespace ca {
 __device__ int g_device_error;
 
 constexpr int kErrTimeout = -4;
+// Shared-memory window not 1024-byte aligned (reported as CA_ERR_CUDA).
+constexpr int kErrLayout = -3;
 // A wait gives up after this many nanoseconds of %globaltimer. No single
 // pipeline step of any launch this library makes comes near it.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
