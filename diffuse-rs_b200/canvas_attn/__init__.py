@@ -22,7 +22,7 @@ from typing import Optional, Sequence
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libcanvas_attn.so")
+LIB_PATH = os.environ.get("CANVAS_ATTN_LIB") or os.path.join(_HERE, "libcanvas_attn.so")
 
 CA_OK = 0
 CA_ERR_INVALID = -1

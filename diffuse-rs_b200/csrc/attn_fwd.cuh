@@ -7,15 +7,13 @@
 // (src/model/attention.rs:35-57, :106-186): per query row, softmax over every
 // visible key of scale * q.k, times V; rows with no visible key give NaN.
 //
-// Warp roles (384 threads):
-//   warp 0      TMA producer: Q once, then K tiles through an ST-stage ring
-//   warp 1      TMEM allocator + tcgen05.mma issuer (one elected lane)
-//   warps 2-3   prologue: build the list of key tiles that have any visible
-//               (query, key) pair, flagging tiles that need per-element masks;
-//               afterwards warp 3 streams V tiles through their own ring
-//   warps 4-11  softmax + O correction + epilogue; TMEM lane r (= row r) is
-//               shared by warps 4 + r/32 and 8 + r/32, each owning half of the
-//               tile's key columns and half of O's columns
+// Warp roles (320 threads, one CTA per SM):
+//   warp 0      lane 0: TMA producer of Q and the K ring; lane 1: the V ring
+//   warp 1      TMEM allocator + tcgen05.mma issuer (lane 0)
+//   warps 0-1   prologue: build the list of key tiles that have any visible
+//               (query, key) pair, flagging tiles that need per-element masks
+//   warps 2-9   softmax, O correction and epilogue in two groups of four
+//               warps (2-5 and 6-9); warp w reaches TMEM lanes 32 (w % 4)..+31
 //
 // Pipeline per visible key tile j (S double-buffered in TMEM, P in smem):
 //   S[j&1] = Q K_j^T           (tcgen05.mma, SS, fp32 accumulate in TMEM)
@@ -35,7 +33,22 @@
 namespace ca {
 
 constexpr int kNoWindow = INT_MAX;
-constexpr int kFwdThreads = 384;  // 4 control warps + 8 softmax warps
+
+// Pipeline event timestamps of one CTA, compiled in only with -DCA_TRACE
+// (a diagnostic build; the product library never records them).
+#ifdef CA_TRACE
+__device__ long long g_trace[16][64];
+#define CA_EV(kind, j)                                                              \
+  do {                                                                              \
+    if (blockIdx.x == 5 && blockIdx.y == 3 && blockIdx.z == 1 && (j) < 64)          \
+      g_trace[kind][j] = clock64();                                                 \
+  } while (0)
+#else
+#define CA_EV(kind, j) \
+  do {                 \
+  } while (0)
+#endif
+constexpr int kFwdThreads = 320;  // 2 control warps + 8 softmax warps
 
 struct FwdParams {
   void* out;
@@ -69,14 +82,23 @@ struct FwdCfg {
   // weights reach the tensor core with ~16 significant bits instead of 8.
   static constexpr bool PRECISE = PRECISE_;
   static constexpr int kPTerms = PRECISE ? 2 : 1;
+  // ALT (alternating tiles): when TMEM holds two S buffers and two O
+  // accumulators, softmax warpgroup g owns key tiles g, g+2, g+4, ... with its
+  // own S buffer, P buffer, O accumulator and running max/sum; the two
+  // partial results are merged once at the end. Otherwise (head_dim 256) both
+  // groups work on every tile, each on half of its columns, and exchange row
+  // maxima per tile.
+  static constexpr bool ALT = 2 * BN + 2 * HDP <= 512;
+  static constexpr int kGroupsP = ALT ? 2 : 1;  // P buffers
   static constexpr int kChunks = HDP / 64;  // 128-byte swizzle atoms along head_dim
   static constexpr int kQChunk = 128 * 128;
   static constexpr int kKChunk = BN * 128;
   static constexpr int kPChunk = 128 * 128;
   static constexpr int kQBytes = kChunks * kQChunk;
   static constexpr int kKVBytes = kChunks * kKChunk;
-  static constexpr int kPBytes = kPTerms * (BN / 64) * kPChunk;
   static constexpr int kPTermBytes = (BN / 64) * kPChunk;
+  static constexpr int kPGroupBytes = kPTerms * kPTermBytes;
+  static constexpr int kPBytes = kGroupsP * kPGroupBytes;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;
   static constexpr int kOffV = kOffK + ST * kKVBytes;
@@ -91,23 +113,27 @@ struct FwdCfg {
   static constexpr int kBarKE = kBarV + ST;   // [ST] K stage free
   static constexpr int kBarVE = kBarKE + ST;  // [ST] V stage free
   static constexpr int kBarS = kBarVE + ST;   // [2] S buffer holds Q K^T
-  static constexpr int kBarP = kBarS + 2;     // P written (8 softmax warps)
-  static constexpr int kBarO = kBarP + 1;     // P V of the latest tile done
-  static constexpr int kBarF = kBarO + 1;     // all MMAs done
+  static constexpr int kBarP = kBarS + 2;     // [2] P written (per P buffer)
+  static constexpr int kBarO = kBarP + 2;     // [2] P V done (per O accumulator)
+  static constexpr int kBarF = kBarO + 2;     // all MMAs done
   static constexpr int kBarX = kBarF + 1;     // [4] softmax warp-pair exchange
   static constexpr int kNumBars = kBarX + 4;
   // Largest key-tile count per sequence (keys <= kMaxTiles * BN).
   static constexpr int kMaxTiles = (PRECISE && HDP == 256) ? 256 : 1024;
   static constexpr int kOffList = kOffBar + kNumBars * 8;
-  static constexpr int kOffXch = kOffList + kMaxTiles * 2;  // float [parity][half][128]
-  static constexpr int kOffMisc = kOffXch + 2 * 2 * 128 * 4;
+  // Warp-pair exchange, float [parity][half][128]. With ALT it is used once,
+  // after the last P V, and lives in the then idle P buffers.
+  static constexpr int kXchBytes = 2 * 2 * 128 * 4;
+  static constexpr int kOffXch = ALT ? kOffP : kOffList + kMaxTiles * 2;
+  static constexpr int kOffMisc = kOffList + kMaxTiles * 2 + (ALT ? 0 : kXchBytes);
   static constexpr int kMiscBytes = 64;
   static constexpr int kSmemBytes = kOffMisc + kMiscBytes;
   static constexpr int kTmemCols = 512;
-  static constexpr int kOCol = 2 * BN;  // O accumulator columns [2BN, 2BN + HDP)
+  static constexpr int kOCol = 2 * BN;  // O accumulator(s) from column 2BN
   static constexpr uint32_t kIdescS = umma_idesc_bf16(128, BN, 0, 0);
   static constexpr uint32_t kIdescO = umma_idesc_bf16(128, HDP, 0, 1);
-  static_assert(kOCol + HDP <= kTmemCols, "TMEM budget");
+  static_assert(kOCol + (ALT ? 2 : 1) * HDP <= kTmemCols, "TMEM budget");
+  static_assert(!ALT || kPBytes >= kXchBytes, "exchange fits in the P buffers");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 256, "tile shape");
 };
@@ -261,6 +287,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST;
+  constexpr bool ALT = C::ALT;
   // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
   // static shared memory, so the dynamic window starts 1024-aligned; if it
   // ever did not, report it instead of computing garbage.
@@ -297,10 +324,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(bar(C::kBarKE + s), 1);
       mbar_init(bar(C::kBarVE + s), 1);
     }
-    mbar_init(bar(C::kBarS), 1);
-    mbar_init(bar(C::kBarS + 1), 1);
-    mbar_init(bar(C::kBarP), 8);
-    mbar_init(bar(C::kBarO), 1);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(bar(C::kBarS + g), 1);
+      mbar_init(bar(C::kBarP + g), ALT ? 4 : 8);
+      mbar_init(bar(C::kBarO + g), 1);
+    }
     mbar_init(bar(C::kBarF), 1);
     for (int i = 0; i < 4; ++i) mbar_init(bar(C::kBarX + i), 2);
     fence_barrier_init();
@@ -315,9 +343,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tmem_alloc(smem_u32(misc), C::kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 2 || warp == 3) {
-    build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, qtile, list, misc, tid - 64);
-  }
+  if (warp <= 1) build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, qtile, list, misc, tid);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -325,12 +351,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int n = misc[1];
   bool dead = false;
 
-  if (warp == 0 || warp == 3) {
+  if (warp == 0) {
     // ------------------------------------------------------------ producers
-    // Warp 0 streams Q and the K tiles, warp 3 the V tiles: the two rings
+    // Lane 0 streams Q and the K tiles, lane 1 the V tiles: the two rings
     // drain at different times (K after Q K^T, V after P V).
-    if (lane == 0) {
-      const bool is_k = warp == 0;
+    if (lane < 2) {
+      const bool is_k = lane == 0;
       const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
       const uint32_t ring = is_k ? sK : sV;
       const int full = is_k ? C::kBarK : C::kBarV;
@@ -346,6 +372,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int s = j % ST;
         if (j >= ST && !mbar_wait(bar(empty + s), ((j / ST) - 1) & 1, dead)) break;
         const int krow = k_beg + (list[j] & 0x7fff) * BN;
+        CA_EV(is_k ? 0 : 1, j);
         mbar_arrive_expect_tx(bar(full + s), C::kKVBytes);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
@@ -361,22 +388,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(bar(C::kBarP), i & 1, dead)) return false;
+        const int g = ALT ? (i & 1) : 0;         // P buffer / O accumulator
+        const int use = ALT ? (i >> 1) : i;      // uses of that buffer so far
+        if (!mbar_wait(bar(C::kBarP + g), use & 1, dead)) return false;
+        CA_EV(3, i);
         const int s = i % ST;
         if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead)) return false;
+        CA_EV(4, i);
         tc_fence_after();
         const uint32_t vbase = sV + s * C::kKVBytes;
+        const uint32_t pbase = sP + g * C::kPGroupBytes;
+        const uint32_t dst = tmem + C::kOCol + g * HDP;
 #pragma unroll
         for (int term = 0; term < C::kPTerms; ++term) {
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             const uint64_t a = umma_desc_sw128(
-                sP + term * C::kPTermBytes + (kk >> 2) * C::kPChunk + (kk & 3) * 32, 16, 1024);
+                pbase + term * C::kPTermBytes + (kk >> 2) * C::kPChunk + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = umma_desc_sw128(vbase + kk * 2048, C::kKChunk, 1024);
-            umma_ss(tmem + C::kOCol, a, bd, C::kIdescO, (i > 0 || kk > 0 || term > 0) ? 1u : 0u);
+            umma_ss(dst, a, bd, C::kIdescO, (use > 0 || kk > 0 || term > 0) ? 1u : 0u);
           }
         }
-        umma_commit(bar(C::kBarO));
+        CA_EV(11, i);
+        umma_commit(bar(C::kBarO + g));
         umma_commit(bar(C::kBarVE + s));
         return true;
       };
@@ -384,6 +418,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int j = 0; j < n; ++j) {
           const int s = j % ST;
           if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) break;
+          CA_EV(2, j);
           tc_fence_after();
           const uint32_t kbase = sK + s * C::kKVBytes;
           const uint32_t sdst = tmem + (j & 1) * BN;
@@ -393,6 +428,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const uint64_t bd = umma_desc_sw128(kbase + (kk >> 2) * C::kKChunk + (kk & 3) * 32, 16, 1024);
             umma_ss(sdst, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
           }
+          CA_EV(10, j);
           umma_commit(bar(C::kBarS + (j & 1)));
           umma_commit(bar(C::kBarKE + s));
           if (j >= 1 && !issue_pv(j - 1)) break;
@@ -404,19 +440,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       bool d2 = false;
       mbar_wait(bar(C::kBarF), 0, d2);
     }
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------------------ softmax
-    // Warps w and w+4 share TMEM lane quarter wq (rows 32wq..32wq+31); `half`
-    // picks which half of each tile's key columns (and of O's columns) the
-    // warp owns. Row maxima and sums are combined through shared memory.
-    constexpr int BH = BN / 2;   // S columns per warp
-    constexpr int OH = HDP / 2;  // O columns per warp
-    const int sw = warp - 4;
-    const int wq = sw & 3;
-    const int half = sw >> 2;
+    // Warps 2..9: warp w reaches TMEM lanes 32 (w % 4) .. +31, so each lane
+    // quarter q has two warps, one per group (grp 0: warps 2-5, 1: 6-9). With ALT, group g owns
+    // key tiles g, g+2, ... (whole rows, its own S/P/O); otherwise both groups
+    // see every tile and own half of its key columns and half of O.
+    constexpr int SC = ALT ? BN : BN / 2;    // S columns per thread per tile
+    constexpr int OC = ALT ? HDP : HDP / 2;  // O columns this group owns
+    const int wq = warp & 3;
+    const int grp = (warp - 2) >> 2;
     const int r = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    float* xch = reinterpret_cast<float*>(smem + C::kOffXch);  // [parity][half][128]
+    const int s_col0 = ALT ? 0 : grp * SC;
+    const uint32_t o_own = C::kOCol + grp * OC;
+    const int pg = ALT ? grp : 0;
+    const uint32_t pbuf = sP + pg * C::kPGroupBytes;
     const uint32_t xbar = bar(C::kBarX + wq);
     const int t_local = qtile * p.QT + r / p.G;
     const bool row_valid = r < p.R && t_local < q_len;
@@ -430,69 +469,83 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const float sl2 = p.scale_log2;
     const bool fast_ok = p.softcap == 0.f && sl2 >= 0.f;
     float m = -INFINITY, l = 0.f;
+    int used = 0;  // tiles this thread has processed
 
-    for (int j = 0; j < n; ++j) {
+    for (int j = ALT ? grp : 0; j < n; j += ALT ? 2 : 1) {
       const int entry = list[j];
       const int kt = entry & 0x7fff;
       const bool partial = (entry & 0x8000) != 0;
       mbar_wait(bar(C::kBarS + (j & 1)), (j >> 1) & 1, dead);
       dead = __any_sync(0xffffffffu, dead);
       if (dead) break;
+      if (warp == 4 && lane == 0) CA_EV(5, j);
       tc_fence_after();
-      uint32_t sr[BH];
-#pragma unroll
-      for (int c = 0; c < BH / 32; ++c)
-        tmem_ld32(tmem + lane_off + (j & 1) * BN + half * BH + c * 32,
-                  *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-      tmem_wait_ld();
-
-      // Partial row max over this warp's columns (8 independent chains: one
-      // warp per SM sub-partition cannot hide a long dependent chain).
-      float pmax;
+      // S is read from TMEM twice, LB columns at a time: pass 1 forms the row
+      // max, pass 2 exponentiates and stores P. No thread ever holds a whole
+      // 128-key row, which keeps the softmax warps within 168 registers.
+      constexpr int LB = 32;  // columns per TMEM load; chunk loops stay rolled (code size)
+      const uint32_t s_addr = tmem + lane_off + (j & 1) * BN + s_col0;
       const bool fast = fast_ok && !partial;
+      // Scaled log2-domain logit of column i (masked keys -> -inf); used only
+      // off the fast path (partial tiles, soft-cap, negative scale).
+      auto logit = [&](uint32_t bits, int i) -> float {
+        float t;
+        if (p.softcap != 0.f) {
+          const float x = u2f(bits) * p.scale;
+          t = p.softcap * tanh_via_exp2(x / p.softcap) * 1.4426950408889634f;
+        } else {
+          t = u2f(bits) * sl2;
+        }
+        if (partial) {
+          const int kl = kt * BN + s_col0 + i;
+          bool ok = kl < k_len;
+          if (ok && p.any_mask) {
+            const int g = k_beg + kl;
+            const int kp = p.k_pos ? p.k_pos[g] : kl;
+            const int ks = p.k_seq ? p.k_seq[g] : 0;
+            ok = visible_dev(qpos, kp, qseq, ks, p.window, qpre);
+          }
+          if (!ok) t = -INFINITY;
+        }
+        return t;
+      };
+
+      // Pass 1: row max over this thread's columns (8 independent chains).
+      float rmax;
       {
         float mx8[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
-        if (fast) {
+#pragma unroll 1
+        for (int cb = 0; cb < SC / LB; ++cb) {
+          uint32_t sr[LB];
 #pragma unroll
-          for (int i = 0; i < BH; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], u2f(sr[i]));
-        } else {
+          for (int c = 0; c < LB / 32; ++c)
+            tmem_ld32(s_addr + cb * LB + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+          tmem_wait_ld();
+          if (fast) {
 #pragma unroll
-          for (int i = 0; i < BH; ++i) {
-            float t;
-            if (p.softcap != 0.f) {
-              const float x = u2f(sr[i]) * p.scale;
-              t = p.softcap * tanh_via_exp2(x / p.softcap) * 1.4426950408889634f;
-            } else {
-              t = u2f(sr[i]) * sl2;
-            }
-            if (partial) {
-              const int kl = kt * BN + half * BH + i;
-              bool ok = kl < k_len;
-              if (ok && p.any_mask) {
-                const int g = k_beg + kl;
-                const int kp = p.k_pos ? p.k_pos[g] : kl;
-                const int ks = p.k_seq ? p.k_seq[g] : 0;
-                ok = visible_dev(qpos, kp, qseq, ks, p.window, qpre);
-              }
-              if (!ok) t = -INFINITY;
-            }
-            sr[i] = f2u(t);
-            mx8[i & 7] = fmaxf(mx8[i & 7], t);
+            for (int i = 0; i < LB; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], u2f(sr[i]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < LB; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], logit(sr[i], cb * LB + i));
           }
         }
-        pmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+        rmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       }
-      // Exchange with the partner warp (same rows, other columns).
-      xch[((j & 1) * 2 + half) * 128 + r] = pmax;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(xbar);
-      mbar_wait(xbar, j & 1, dead);
-      dead = __any_sync(0xffffffffu, dead);
-      if (dead) break;
-      const float rmax = fmaxf(pmax, xch[((j & 1) * 2 + (half ^ 1)) * 128 + r]);
+      if (warp == 4 && lane == 0) CA_EV(6, j);
+      if constexpr (!ALT) {
+        // Combine with the partner warp (same rows, other key columns).
+        float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
+        xch[((j & 1) * 2 + grp) * 128 + r] = rmax;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xbar);
+        mbar_wait(xbar, j & 1, dead);
+        dead = __any_sync(0xffffffffu, dead);
+        if (dead) break;
+        rmax = fmaxf(rmax, xch[((j & 1) * 2 + (grp ^ 1)) * 128 + r]);
+      }
       const float mcand = fast ? rmax * sl2 : rmax;
 
       const bool resc = mcand > m + 8.f;
@@ -502,115 +555,183 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         m = mcand;
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[BH / 2];
-      uint32_t pl[C::PRECISE ? BH / 2 : 1];
-#pragma unroll
-      for (int i = 0; i < BH; i += 2) {
-        float p0, p1;
-        if (fast) {
-          p0 = ex2_approx(fmaf(u2f(sr[i]), sl2, -mu));
-          p1 = ex2_approx(fmaf(u2f(sr[i + 1]), sl2, -mu));
-        } else {
-          p0 = ex2_approx(u2f(sr[i]) - mu);
-          p1 = ex2_approx(u2f(sr[i + 1]) - mu);
-        }
-        sum4[(i >> 1) & 3] += p0 + p1;
-        pk[i / 2] = pack_bf16(p0, p1);
-        if constexpr (C::PRECISE) {
-          const float h0 = __uint_as_float(pk[i / 2] << 16);
-          const float h1 = __uint_as_float(pk[i / 2] & 0xffff0000u);
-          pl[i / 2] = pack_bf16(p0 - h0, p1 - h1);
-        }
-      }
-      l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
 
-      // P's buffer and O are free once P V of the previous tile completed.
-      if (j > 0) {
-        mbar_wait(bar(C::kBarO), (j - 1) & 1, dead);
+      // This group's P buffer and O are free once its previous P V completed
+      // (with ALT that was issued a whole group period ago).
+      if (used > 0) {
+        mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
         dead = __any_sync(0xffffffffu, dead);
         if (dead) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, resc)) {
+      }
+      if (warp == 4 && lane == 0) CA_EV(7, j);
+      // Pass 2: exponentiate 8 keys at a time and store them straight into P
+      // (row r: 128-byte rows of 64 keys, 16-byte units XOR-swizzled by r & 7).
+      // The fast and the masked/soft-capped forms are separate loops so the
+      // hot one carries no code of the other.
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      auto store_p = [&](int key0, const uint32_t (&pk)[4], const uint32_t (&pl)[4]) {
+        const uint32_t addr =
+            pbuf + (key0 >> 6) * C::kPChunk + r * 128 + ((((key0 & 63) >> 3) ^ (r & 7)) << 4);
+        st_shared_v4(addr, pk[0], pk[1], pk[2], pk[3]);
+        if constexpr (C::PRECISE) st_shared_v4(addr + C::kPTermBytes, pl[0], pl[1], pl[2], pl[3]);
+      };
+      auto emit = [&](float p0, float p1, int q2, uint32_t (&pk)[4], uint32_t (&pl)[4]) {
+        sum4[q2] += p0 + p1;
+        pk[q2] = pack_bf16(p0, p1);
+        if constexpr (C::PRECISE) {
+          const float h0 = __uint_as_float(pk[q2] << 16);
+          const float h1 = __uint_as_float(pk[q2] & 0xffff0000u);
+          pl[q2] = pack_bf16(p0 - h0, p1 - h1);
+        }
+      };
+      if (fast) {
 #pragma unroll 1
-          for (int c = 0; c < OH / 32; ++c) {
-            uint32_t o[32];
-            const uint32_t ta = tmem + lane_off + C::kOCol + half * OH + c * 32;
-            tmem_ld32(ta, o);
-            tmem_wait_ld();
+        for (int cb = 0; cb < SC / LB; ++cb) {
+          uint32_t sr[LB];
+          tmem_ld32(s_addr + cb * LB, sr);
+          tmem_wait_ld();
+          if (warp == 4 && lane == 0 && cb == 0) CA_EV(12, j);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * corr);
-            tmem_st32(ta, o);
+          for (int u = 0; u < LB / 8; ++u) {
+            uint32_t pk[4], pl[4];
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) {
+              const int i = u * 8 + q2 * 2;
+              emit(ex2_approx(fmaf(u2f(sr[i]), sl2, -mu)),
+                   ex2_approx(fmaf(u2f(sr[i + 1]), sl2, -mu)), q2, pk, pl);
+            }
+            store_p(s_col0 + cb * LB + u * 8, pk, pl);
           }
-          tmem_wait_st();
+          if (warp == 4 && lane == 0 && cb == 0) CA_EV(13, j);
+        }
+      } else {
+#pragma unroll 1
+        for (int cb = 0; cb < SC / LB; ++cb) {
+          uint32_t sr[LB];
+          tmem_ld32(s_addr + cb * LB, sr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < LB / 8; ++u) {
+            uint32_t pk[4], pl[4];
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) {
+              const int i = u * 8 + q2 * 2;
+              emit(ex2_approx(logit(sr[i], cb * LB + i) - mu),
+                   ex2_approx(logit(sr[i + 1], cb * LB + i + 1) - mu), q2, pk, pl);
+            }
+            store_p(s_col0 + cb * LB + u * 8, pk, pl);
+          }
         }
       }
-      // P row r: 128-byte rows of 64 keys, 16-byte units XOR-swizzled by (r & 7).
+      l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+      if (warp == 4 && lane == 0) CA_EV(8, j);
+      // Lazy correction of O (rare after the first tiles), once S is dead.
+      if (used > 0 && __any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+        for (int c = 0; c < OC / 32; ++c) {
+          uint32_t o[32];
+          const uint32_t ta = tmem + lane_off + o_own + c * 32;
+          tmem_ld32(ta, o);
+          tmem_wait_ld();
 #pragma unroll
-      for (int u = 0; u < BH / 8; ++u) {
-        const int key0 = half * BH + u * 8;
-        const uint32_t addr =
-            sP + (key0 >> 6) * C::kPChunk + r * 128 + ((((key0 & 63) >> 3) ^ (r & 7)) << 4);
-        st_shared_v4(addr, pk[u * 4], pk[u * 4 + 1], pk[u * 4 + 2], pk[u * 4 + 3]);
-        if constexpr (C::PRECISE)
-          st_shared_v4(addr + C::kPTermBytes, pl[u * 4], pl[u * 4 + 1], pl[u * 4 + 2],
-                       pl[u * 4 + 3]);
+          for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * corr);
+          tmem_st32(ta, o);
+        }
+        tmem_wait_st();
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::kBarP));
+      if (warp == 4 && lane == 0) CA_EV(9, j);
+      if (lane == 0) mbar_arrive(bar(C::kBarP + pg));
+      ++used;
     }
 
     // ------------------------------------------------------------ epilogue
-    bool have_o = n > 0 && !dead;
-    if (have_o) {
-      mbar_wait(bar(C::kBarO), (n - 1) & 1, dead);
+    // Wait for this group's last P V, then combine with the partner warp:
+    // ALT merges two (max, sum, O) partials; otherwise the row sums add.
+    if (used > 0 && !dead) {
+      mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
       dead = __any_sync(0xffffffffu, dead);
-      have_o = !dead;
-      tc_fence_after();
     }
-    if (have_o) {  // row sum = both halves' partial sums (same running max)
-      xch[((n & 1) * 2 + half) * 128 + r] = l;
+    float* xo = ALT ? reinterpret_cast<float*>(smem + C::kOffP + grp * C::kPGroupBytes)
+                    : reinterpret_cast<float*>(smem + C::kOffXch) + ((n & 1) * 2 + grp) * 128;
+    float* xp = ALT ? reinterpret_cast<float*>(smem + C::kOffP + (grp ^ 1) * C::kPGroupBytes)
+                    : reinterpret_cast<float*>(smem + C::kOffXch) + ((n & 1) * 2 + (grp ^ 1)) * 128;
+    const int parity = ALT ? 0 : (n & 1);
+    bool have = n > 0 && !dead;
+    float s_me = 1.f, s_ot = 0.f, inv = __int_as_float(0x7fc00000);
+    const int n_me = ALT ? (grp == 0 ? (n + 1) / 2 : n / 2) : n;
+    const int n_ot = ALT ? (grp == 0 ? n / 2 : (n + 1) / 2) : 0;
+    if (have) {
+      xo[r] = l;
+      if (ALT) xo[128 + r] = m;
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
-      mbar_wait(xbar, n & 1, dead);
+      mbar_wait(xbar, parity, dead);
       dead = __any_sync(0xffffffffu, dead);
-      have_o = !dead;
-      l += xch[((n & 1) * 2 + (half ^ 1)) * 128 + r];
+      have = !dead;
+      tc_fence_after();
+      const float l_ot = xp[r];
+      if (ALT) {
+        const float m_ot = xp[128 + r];
+        const float mt = fmaxf(n_me > 0 ? m : -INFINITY, n_ot > 0 ? m_ot : -INFINITY);
+        const float mref = mt == -INFINITY ? 0.f : mt;
+        s_me = n_me > 0 ? ex2_approx(m - mref) : 0.f;
+        s_ot = n_ot > 0 ? ex2_approx(m_ot - mref) : 0.f;
+        const float lt = s_me * (n_me > 0 ? l : 0.f) + s_ot * (n_ot > 0 ? l_ot : 0.f);
+        inv = 1.f / lt;
+      } else {
+        inv = 1.f / (l + l_ot);
+      }
     }
-    const float inv = have_o ? 1.f / l : __int_as_float(0x7fc00000);
     const int head = kvh * p.G + (r % p.G);
+    // Output columns this warp writes: with ALT group g writes columns
+    // [g HDP/2, (g+1) HDP/2) from both accumulators; otherwise its own half.
+    constexpr int WC = HDP / 2;
+    const uint32_t o_me = ALT ? C::kOCol + grp * HDP : o_own;
+    const uint32_t o_ot = C::kOCol + (grp ^ 1) * HDP;
 #pragma unroll 1
-    for (int c = 0; c < OH / 32; ++c) {
+    for (int c = 0; c < WC / 32; ++c) {
+      const int col_base = grp * WC + c * 32;
       uint32_t o[32];
-      if (have_o) {
-        tmem_ld32(tmem + lane_off + C::kOCol + half * OH + c * 32, o);
+      float v[32];
+      if (have && n_me > 0) {
+        tmem_ld32(tmem + lane_off + o_me + (ALT ? col_base : c * 32), o);
         tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = u2f(o[i]) * s_me;
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0u;
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      if (ALT && have && n_ot > 0) {
+        tmem_ld32(tmem + lane_off + o_ot + col_base, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = fmaf(u2f(o[i]), s_ot, v[i]);
       }
       if (row_valid) {
         const int64_t obase = static_cast<int64_t>(gq) * p.out_row_stride +
                               static_cast<int64_t>(head) * p.hd;
 #pragma unroll
         for (int g8 = 0; g8 < 4; ++g8) {
-          const int col = half * OH + c * 32 + g8 * 8;
+          const int col = col_base + g8 * 8;
           if (col < p.hd) {
-            float v[8];
+            float w8[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = have_o ? u2f(o[g8 * 8 + i]) * inv : inv;
+            for (int i = 0; i < 8; ++i) w8[i] = have ? v[g8 * 8 + i] * inv : inv;
             if (p.out_f32) {
               float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase + col);
-              dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-              dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+              dst[0] = make_float4(w8[0], w8[1], w8[2], w8[3]);
+              dst[1] = make_float4(w8[4], w8[5], w8[6], w8[7]);
             } else {
               uint4 w;
-              w.x = pack_bf16(v[0], v[1]);
-              w.y = pack_bf16(v[2], v[3]);
-              w.z = pack_bf16(v[4], v[5]);
-              w.w = pack_bf16(v[6], v[7]);
+              w.x = pack_bf16(w8[0], w8[1]);
+              w.y = pack_bf16(w8[2], w8[3]);
+              w.z = pack_bf16(w8[4], w8[5]);
+              w.w = pack_bf16(w8[6], w8[7]);
               *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + obase + col) = w;
             }
           }

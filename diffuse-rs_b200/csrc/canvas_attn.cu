@@ -173,7 +173,7 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
 
   Launch L{a, &p, total_q, total_k, max_sq, max_sk, qrs, krs, st};
   if (a->precise) {
-    if (hdp == 64) return L.run<FwdCfg<64, 128, 3, true>>();
+    if (hdp == 64) return L.run<FwdCfg<64, 128, 2, true>>();
     if (hdp == 128) return L.run<FwdCfg<128, 64, 3, true>>();
     if (hdp == 192) return L.run<FwdCfg<192, 64, 2, true>>();
     return L.run<FwdCfg<256, 64, 2, true>>();
@@ -481,5 +481,12 @@ const char* ca_status_string(int status) {
 }
 
 const char* ca_version(void) { return "canvas_attn 0.1.0 sm_100a"; }
+
+#ifdef CA_TRACE
+// Diagnostic builds only: copies the recorded event timestamps to `dst`.
+int ca_debug_trace(long long* dst) {
+  return cudaMemcpyFromSymbol(dst, ca::g_trace, sizeof(ca::g_trace)) == cudaSuccess ? 0 : -3;
+}
+#endif
 
 }  // extern "C"

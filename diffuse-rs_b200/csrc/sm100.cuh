@@ -65,6 +65,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or about `ns` nanoseconds pass, leaving the SM sub-
+// partition's issue slots to the warps doing work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Returns false (and
 // records the timeout in g_device_error) if it does not complete within
 // kWaitLimitNs, or immediately if *dead is already set by an earlier expiry.
@@ -72,9 +87,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, bool& d
   if (dead) return false;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  uint32_t spins = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+  while (!mbar_try_wait_sleep(bar, parity, 100000u)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
       atomicExch(&g_device_error, kErrTimeout);
       dead = true;
       return false;
@@ -197,9 +211,13 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn, i
 
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float ex2_approx(float x) {
+#ifdef CA_DIAG_NO_EX2
+  return fmaf(x, 0.0001f, 1.0f);
+#else
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+#endif
 }
 
 // Packs (lo, hi) into one bf16x2 word, lo in the low half, round to nearest.
