@@ -33,6 +33,8 @@
 namespace ca {
 
 constexpr int kNoWindow = INT_MAX;
+// Bit q of kPolyPairs: pair q of every 8 keys uses the FMA-pipe exp2.
+constexpr int kPolyPairs = 0;
 
 // Pipeline event timestamps of one CTA, compiled in only with -DCA_TRACE
 // (a diagnostic build; the product library never records them).
@@ -115,7 +117,8 @@ struct FwdCfg {
   static constexpr int kBarS = kBarVE + ST;   // [2] S buffer holds Q K^T
   static constexpr int kBarP = kBarS + 2;     // [2] P written (per P buffer)
   static constexpr int kBarO = kBarP + 2;     // [2] P V done (per O accumulator)
-  static constexpr int kBarF = kBarO + 2;     // all MMAs done
+  static constexpr int kBarSF = kBarO + 2;    // [2] S buffer read out by softmax
+  static constexpr int kBarF = kBarSF + 2;    // all MMAs done
   static constexpr int kBarX = kBarF + 1;     // [4] softmax warp-pair exchange
   static constexpr int kNumBars = kBarX + 4;
   // Largest key-tile count per sequence (keys <= kMaxTiles * BN).
@@ -328,6 +331,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(bar(C::kBarS + g), 1);
       mbar_init(bar(C::kBarP + g), ALT ? 4 : 8);
       mbar_init(bar(C::kBarO + g), 1);
+      mbar_init(bar(C::kBarSF + g), ALT ? 4 : 8);
     }
     mbar_init(bar(C::kBarF), 1);
     for (int i = 0; i < 4; ++i) mbar_init(bar(C::kBarX + i), 2);
@@ -414,26 +418,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         umma_commit(bar(C::kBarVE + s));
         return true;
       };
-      if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead)) {
-        for (int j = 0; j < n; ++j) {
-          const int s = j % ST;
-          if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) break;
-          CA_EV(2, j);
-          tc_fence_after();
-          const uint32_t kbase = sK + s * C::kKVBytes;
-          const uint32_t sdst = tmem + (j & 1) * BN;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % ST;
+        if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) return false;
+        CA_EV(2, j);
+        tc_fence_after();
+        const uint32_t kbase = sK + s * C::kKVBytes;
+        const uint32_t sdst = tmem + (j & 1) * BN;
 #pragma unroll
-          for (int kk = 0; kk < HDP / 16; ++kk) {
-            const uint64_t a = umma_desc_sw128(sQ + (kk >> 2) * C::kQChunk + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(kbase + (kk >> 2) * C::kKChunk + (kk & 3) * 32, 16, 1024);
-            umma_ss(sdst, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
-          }
-          CA_EV(10, j);
-          umma_commit(bar(C::kBarS + (j & 1)));
-          umma_commit(bar(C::kBarKE + s));
-          if (j >= 1 && !issue_pv(j - 1)) break;
+        for (int kk = 0; kk < HDP / 16; ++kk) {
+          const uint64_t a = umma_desc_sw128(sQ + (kk >> 2) * C::kQChunk + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(kbase + (kk >> 2) * C::kKChunk + (kk & 3) * 32, 16, 1024);
+          umma_ss(sdst, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
         }
-        if (!dead) issue_pv(n - 1);
+        CA_EV(10, j);
+        umma_commit(bar(C::kBarS + (j & 1)));
+        umma_commit(bar(C::kBarKE + s));
+        return true;
+      };
+      // Order: S[0], S[1], then per tile j: S[j+2] as soon as the softmax has
+      // read S[j] out of its buffer, then P V[j] once P[j] is written. The
+      // tensor core thus computes a group's next scores while that group
+      // still exponentiates, instead of after its P V.
+      if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead)) {
+        bool ok = issue_s(0) && (n < 2 || issue_s(1));
+        for (int j = 0; ok && j < n; ++j) {
+          if (j + 2 < n) {
+            ok = mbar_wait(bar(C::kBarSF + (j & 1)), (j >> 1) & 1, dead) && issue_s(j + 2);
+            if (!ok) break;
+          }
+          ok = issue_pv(j);
+        }
       }
       // Every MMA this thread issued completes before the role ends.
       umma_commit(bar(C::kBarF));
@@ -598,8 +613,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int q2 = 0; q2 < 4; ++q2) {
               const int i = u * 8 + q2 * 2;
-              emit(ex2_approx(fmaf(u2f(sr[i]), sl2, -mu)),
-                   ex2_approx(fmaf(u2f(sr[i + 1]), sl2, -mu)), q2, pk, pl);
+              // Pairs selected by kPolyPairs go through the FMA-pipe exp2
+              // (ex2_poly); measured break-even is low, so it is off.
+              const float x0 = fmaf(u2f(sr[i]), sl2, -mu);
+              const float x1 = fmaf(u2f(sr[i + 1]), sl2, -mu);
+              if ((kPolyPairs >> q2) & 1)
+                emit(ex2_poly(x0), ex2_poly(x1), q2, pk, pl);
+              else
+                emit(ex2_approx(x0), ex2_approx(x1), q2, pk, pl);
             }
             store_p(s_col0 + cb * LB + u * 8, pk, pl);
           }
@@ -624,6 +645,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
         }
       }
+      // S[j] is fully read: its buffer may take S[j + 2].
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C::kBarSF + (j & 1)));
       l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
       if (warp == 4 && lane == 0) CA_EV(8, j);
       // Lazy correction of O (rare after the first tiles), once S is dead.

@@ -220,6 +220,32 @@ __device__ __forceinline__ float ex2_approx(float x) {
 #endif
 }
 
+// 2^x on the FMA/ALU pipes, so that part of the softmax exponentials leave
+// the MUFU unit (its 4 lanes per clock per sub-partition bound the softmax).
+// Method: round-to-nearest range reduction x = n + f, |f| <= 1/2, by adding
+// 1.5 * 2^23 (n lands in the low mantissa bits of the sum); 2^f from a degree-5
+// polynomial fitted to 2^f on [-1/2, 1/2] (relative-error least squares at
+// Chebyshev nodes, c0 = 1); 2^n applied by adding n to the exponent field.
+// Max relative error over [-126, 8]: 1.8e-7. Inputs below -126 return 2^-126
+// (callers use it only on finite scores, where such terms are negligible).
+constexpr float kExp2C1 = 0.6931470036506653f;
+constexpr float kExp2C2 = 0.24022242426872253f;
+constexpr float kExp2C3 = 0.05550692602992058f;
+constexpr float kExp2C4 = 0.009671509265899658f;
+constexpr float kExp2C5 = 0.00132767076138407f;
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float p = fmaf(kExp2C5, f, kExp2C4);
+  p = fmaf(p, f, kExp2C3);
+  p = fmaf(p, f, kExp2C2);
+  p = fmaf(p, f, kExp2C1);
+  p = fmaf(p, f, 1.f);
+  const int n = __float_as_int(t) - 0x4B400000;  // bit pattern of 12582912.f
+  return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
 // Packs (lo, hi) into one bf16x2 word, lo in the low half, round to nearest.
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
