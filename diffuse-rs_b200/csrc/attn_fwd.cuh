@@ -75,7 +75,16 @@ struct FwdParams {
   int any_mask;       // any of: positions, seq ids, prefixes, window, causal prefix
 };
 
-template <int HDP_, int BN_, int ST_, bool PRECISE_ = false>
+// Softmax organisation of a CTA (see the file comment):
+//   kSplit  one Q tile; both warp groups see every key tile, each on half of
+//           its key columns and half of O (head_dim 256: TMEM holds one O)
+//   kAlt    one Q tile; group g takes key tiles g, g+2, ... with its own S, P
+//           and O, merged at the end (head_dim 192, or a single Q tile)
+//   kPairQ  two Q tiles sharing every K/V tile; group g owns Q tile g with a
+//           double-buffered S, its own P and O (head_dim <= 128)
+enum FwdMode { kSplit = 0, kAlt = 1, kPairQ = 2 };
+
+template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_>
 struct FwdCfg {
   static constexpr int HDP = HDP_;  // head_dim padded to a multiple of 64
   static constexpr int BN = BN_;    // keys per tile
@@ -83,60 +92,58 @@ struct FwdCfg {
   // PRECISE: P is split into bf16 hi + lo terms (two PV MMAs), so the softmax
   // weights reach the tensor core with ~16 significant bits instead of 8.
   static constexpr bool PRECISE = PRECISE_;
+  static constexpr int MODE = MODE_;
+  static constexpr bool ALT = MODE == kAlt;
+  static constexpr bool PAIRQ = MODE == kPairQ;
+  static constexpr bool SPLIT = MODE == kSplit;
   static constexpr int kPTerms = PRECISE ? 2 : 1;
-  // ALT (alternating tiles): when TMEM holds two S buffers and two O
-  // accumulators, softmax warpgroup g owns key tiles g, g+2, g+4, ... with its
-  // own S buffer, P buffer, O accumulator and running max/sum; the two
-  // partial results are merged once at the end. Otherwise (head_dim 256) both
-  // groups work on every tile, each on half of its columns, and exchange row
-  // maxima per tile.
-  static constexpr bool ALT = 2 * BN + 2 * HDP <= 512;
-  static constexpr int kGroupsP = ALT ? 2 : 1;  // P buffers
+  static constexpr int NQ = PAIRQ ? 2 : 1;       // Q tiles per CTA
+  static constexpr int kGroupsP = SPLIT ? 1 : 2;  // P buffers / O accumulators
+  static constexpr int SB = PAIRQ ? 4 : 2;       // S buffers in TMEM
   static constexpr int kChunks = HDP / 64;  // 128-byte swizzle atoms along head_dim
   static constexpr int kQChunk = 128 * 128;
   static constexpr int kKChunk = BN * 128;
   static constexpr int kPChunk = 128 * 128;
-  static constexpr int kQBytes = kChunks * kQChunk;
+  static constexpr int kQBytes = kChunks * kQChunk;  // one Q tile
   static constexpr int kKVBytes = kChunks * kKChunk;
   static constexpr int kPTermBytes = (BN / 64) * kPChunk;
   static constexpr int kPGroupBytes = kPTerms * kPTermBytes;
   static constexpr int kPBytes = kGroupsP * kPGroupBytes;
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffK = kOffQ + NQ * kQBytes;
   static constexpr int kOffV = kOffK + ST * kKVBytes;
   static constexpr int kOffP = kOffV + ST * kKVBytes;
   static constexpr int kOffBar = kOffP + kPBytes;
   // Barriers. K and V stages are released separately: a K stage as soon as
-  // its Q K^T MMA completes, a V stage when its P V MMA completes, so the
-  // next key tile's load overlaps the current tile's softmax.
+  // its Q K^T MMA(s) complete, a V stage when its P V MMA(s) complete.
   static constexpr int kBarQ = 0;
   static constexpr int kBarK = 1;             // [ST] K tile landed
   static constexpr int kBarV = kBarK + ST;    // [ST] V tile landed
   static constexpr int kBarKE = kBarV + ST;   // [ST] K stage free
   static constexpr int kBarVE = kBarKE + ST;  // [ST] V stage free
-  static constexpr int kBarS = kBarVE + ST;   // [2] S buffer holds Q K^T
-  static constexpr int kBarP = kBarS + 2;     // [2] P written (per P buffer)
+  static constexpr int kBarS = kBarVE + ST;   // [SB] S buffer holds Q K^T
+  static constexpr int kBarSF = kBarS + SB;   // [SB] S buffer read out by softmax
+  static constexpr int kBarP = kBarSF + SB;   // [2] P written (per P buffer)
   static constexpr int kBarO = kBarP + 2;     // [2] P V done (per O accumulator)
-  static constexpr int kBarSF = kBarO + 2;    // [2] S buffer read out by softmax
-  static constexpr int kBarF = kBarSF + 2;    // all MMAs done
+  static constexpr int kBarF = kBarO + 2;     // all MMAs done
   static constexpr int kBarX = kBarF + 1;     // [4] softmax warp-pair exchange
   static constexpr int kNumBars = kBarX + 4;
   // Largest key-tile count per sequence (keys <= kMaxTiles * BN).
   static constexpr int kMaxTiles = (PRECISE && HDP == 256) ? 256 : 1024;
   static constexpr int kOffList = kOffBar + kNumBars * 8;
-  // Warp-pair exchange, float [parity][half][128]. With ALT it is used once,
-  // after the last P V, and lives in the then idle P buffers.
+  // Warp-pair exchange, float [parity][half][128]. Outside kSplit it is used
+  // once, after the last P V, and lives in the then idle P buffers.
   static constexpr int kXchBytes = 2 * 2 * 128 * 4;
-  static constexpr int kOffXch = ALT ? kOffP : kOffList + kMaxTiles * 2;
-  static constexpr int kOffMisc = kOffList + kMaxTiles * 2 + (ALT ? 0 : kXchBytes);
+  static constexpr int kOffXch = SPLIT ? kOffList + kMaxTiles * 2 : kOffP;
+  static constexpr int kOffMisc = kOffList + kMaxTiles * 2 + (SPLIT ? kXchBytes : 0);
   static constexpr int kMiscBytes = 64;
   static constexpr int kSmemBytes = kOffMisc + kMiscBytes;
   static constexpr int kTmemCols = 512;
-  static constexpr int kOCol = 2 * BN;  // O accumulator(s) from column 2BN
+  static constexpr int kOCol = SB * BN;  // O accumulator(s) after the S buffers
   static constexpr uint32_t kIdescS = umma_idesc_bf16(128, BN, 0, 0);
   static constexpr uint32_t kIdescO = umma_idesc_bf16(128, HDP, 0, 1);
-  static_assert(kOCol + (ALT ? 2 : 1) * HDP <= kTmemCols, "TMEM budget");
-  static_assert(!ALT || kPBytes >= kXchBytes, "exchange fits in the P buffers");
+  static_assert(kOCol + (SPLIT ? 1 : 2) * HDP <= kTmemCols, "TMEM budget");
+  static_assert(SPLIT || kPBytes >= kXchBytes, "exchange fits in the P buffers");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 256, "tile shape");
 };
@@ -194,7 +201,7 @@ __device__ __forceinline__ void seq_range(const FwdParams& p, int b, int& q_beg,
 // and then compacted; misc[1] receives the count.
 template <class C>
 __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_beg, int k_len,
-                                int qtile, uint16_t* list, int* misc, int tid64) {
+                                int t0, int span, uint16_t* list, int* misc, int tid64) {
   uint16_t* flags = list;
   const int lane = tid64 & 31;
   const int w = tid64 >> 5;  // 0..1
@@ -210,8 +217,7 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
       qs[4] = INT_MAX; qs[5] = 0; qs[6] = 0;
     }
     named_bar_sync(1, 64);
-    const int t0 = qtile * p.QT;
-    const int nt = min(p.QT, q_len - t0);
+    const int nt = min(span, q_len - t0);  // query tokens of this CTA
     for (int t = tid64; t < nt; t += 64) {
       const int tl = t0 + t;
       const int g = q_beg + tl;
@@ -289,8 +295,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
-  constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST;
-  constexpr bool ALT = C::ALT;
+  constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST, NQ = C::NQ;
+  constexpr bool ALT = C::ALT, PAIRQ = C::PAIRQ, SPLIT = C::SPLIT;
   // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
   // static shared memory, so the dynamic window starts 1024-aligned; if it
   // ever did not, report it instead of computing garbage.
@@ -302,13 +308,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int qtile = blockIdx.x;
+  const int qtile = blockIdx.x;  // index of this CTA's group of NQ query tiles
   const int kvh = blockIdx.y;
   const int b = blockIdx.z;
 
   int q_beg, q_len, k_beg, k_len;
   seq_range(p, b, q_beg, q_len, k_beg, k_len);
-  if (qtile * p.QT >= q_len) return;  // uniform across the CTA
+  const int t0 = qtile * NQ * p.QT;  // first query token of this CTA
+  if (t0 >= q_len) return;           // uniform across the CTA
 
   const uint32_t sQ = smem_u32(smem + C::kOffQ);
   const uint32_t sK = smem_u32(smem + C::kOffK);
@@ -327,11 +334,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(bar(C::kBarKE + s), 1);
       mbar_init(bar(C::kBarVE + s), 1);
     }
+    for (int i = 0; i < C::SB; ++i) {
+      mbar_init(bar(C::kBarS + i), 1);
+      mbar_init(bar(C::kBarSF + i), SPLIT ? 8 : 4);
+    }
     for (int g = 0; g < 2; ++g) {
-      mbar_init(bar(C::kBarS + g), 1);
-      mbar_init(bar(C::kBarP + g), ALT ? 4 : 8);
+      mbar_init(bar(C::kBarP + g), SPLIT ? 8 : 4);
       mbar_init(bar(C::kBarO + g), 1);
-      mbar_init(bar(C::kBarSF + g), ALT ? 4 : 8);
     }
     mbar_init(bar(C::kBarF), 1);
     for (int i = 0; i < 4; ++i) mbar_init(bar(C::kBarX + i), 2);
@@ -347,7 +356,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tmem_alloc(smem_u32(misc), C::kTmemCols);
     tmem_relinquish();
   }
-  if (warp <= 1) build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, qtile, list, misc, tid);
+  if (warp <= 1)
+    build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, t0, NQ * p.QT, list, misc, tid);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -366,11 +376,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int full = is_k ? C::kBarK : C::kBarV;
       const int empty = is_k ? C::kBarKE : C::kBarVE;
       if (is_k) {
-        const int q_tok0 = q_beg + qtile * p.QT;
-        mbar_arrive_expect_tx(bar(C::kBarQ), C::kChunks * 128u * p.R);
+        mbar_arrive_expect_tx(bar(C::kBarQ), NQ * C::kChunks * 128u * p.R);
 #pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sQ + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64, kvh * p.G, q_tok0);
+        for (int t = 0; t < NQ; ++t)
+#pragma unroll
+          for (int c = 0; c < C::kChunks; ++c)
+            tma_load_3d(sQ + t * C::kQBytes + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64,
+                        kvh * p.G, q_beg + t0 + t * p.QT);
       }
       for (int j = 0; j < n; ++j) {
         const int s = j % ST;
@@ -391,16 +403,39 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      auto issue_pv = [&](int i) -> bool {
-        const int g = ALT ? (i & 1) : 0;         // P buffer / O accumulator
-        const int use = ALT ? (i >> 1) : i;      // uses of that buffer so far
+      // S buffer of (tile j, Q tile g), and how often it was used before.
+      auto sbuf = [&](int j, int g) -> int { return PAIRQ ? g * 2 + (j & 1) : (j & 1); };
+      // Q K^T of tile j for Q tile g (waits for the buffer's previous reader).
+      auto mma_s = [&](int j, int g, uint32_t kbase) -> bool {
+        const int sb = sbuf(j, g);
+        if (j >= 2 && !mbar_wait(bar(C::kBarSF + sb), ((j - 2) >> 1) & 1, dead)) return false;
+        tc_fence_after();
+        const uint32_t qbase = sQ + g * C::kQBytes;
+#pragma unroll
+        for (int kk = 0; kk < HDP / 16; ++kk) {
+          const uint64_t a = umma_desc_sw128(qbase + (kk >> 2) * C::kQChunk + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(kbase + (kk >> 2) * C::kKChunk + (kk & 3) * 32, 16, 1024);
+          umma_ss(tmem + sb * BN, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(C::kBarS + sb));
+        return true;
+      };
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % ST;
+        if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) return false;
+        CA_EV(2, j);
+        const uint32_t kbase = sK + s * C::kKVBytes;
+        for (int g = 0; g < NQ; ++g)
+          if (!mma_s(j, g, kbase)) return false;
+        CA_EV(10, j);
+        umma_commit(bar(C::kBarKE + s));
+        return true;
+      };
+      // P V of tile j into accumulator g (P buffer g).
+      auto mma_pv = [&](int i, int g, int use, uint32_t vbase) -> bool {
         if (!mbar_wait(bar(C::kBarP + g), use & 1, dead)) return false;
         CA_EV(3, i);
-        const int s = i % ST;
-        if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead)) return false;
-        CA_EV(4, i);
         tc_fence_after();
-        const uint32_t vbase = sV + s * C::kKVBytes;
         const uint32_t pbase = sP + g * C::kPGroupBytes;
         const uint32_t dst = tmem + C::kOCol + g * HDP;
 #pragma unroll
@@ -413,41 +448,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             umma_ss(dst, a, bd, C::kIdescO, (use > 0 || kk > 0 || term > 0) ? 1u : 0u);
           }
         }
-        CA_EV(11, i);
         umma_commit(bar(C::kBarO + g));
+        return true;
+      };
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % ST;
+        if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead)) return false;
+        CA_EV(4, i);
+        const uint32_t vbase = sV + s * C::kKVBytes;
+        if (PAIRQ) {
+          for (int g = 0; g < 2; ++g)
+            if (!mma_pv(i, g, i, vbase)) return false;
+        } else if (ALT) {
+          if (!mma_pv(i, i & 1, i >> 1, vbase)) return false;
+        } else {
+          if (!mma_pv(i, 0, i, vbase)) return false;
+        }
+        CA_EV(11, i);
         umma_commit(bar(C::kBarVE + s));
         return true;
       };
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % ST;
-        if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) return false;
-        CA_EV(2, j);
-        tc_fence_after();
-        const uint32_t kbase = sK + s * C::kKVBytes;
-        const uint32_t sdst = tmem + (j & 1) * BN;
-#pragma unroll
-        for (int kk = 0; kk < HDP / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(sQ + (kk >> 2) * C::kQChunk + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(kbase + (kk >> 2) * C::kKChunk + (kk & 3) * 32, 16, 1024);
-          umma_ss(sdst, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
-        }
-        CA_EV(10, j);
-        umma_commit(bar(C::kBarS + (j & 1)));
-        umma_commit(bar(C::kBarKE + s));
-        return true;
-      };
-      // Order: S[0], S[1], then per tile j: S[j+2] as soon as the softmax has
-      // read S[j] out of its buffer, then P V[j] once P[j] is written. The
-      // tensor core thus computes a group's next scores while that group
-      // still exponentiates, instead of after its P V.
+      // Order: S[0], S[1], then per tile j: P V[j] once P[j] is written and
+      // S[j+2] once the softmax has read S[j] out of its buffer (with PAIRQ
+      // each Q tile has two S buffers, so S[j+1] is already computing while
+      // the group works on S[j]).
       if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead)) {
-        bool ok = issue_s(0) && (n < 2 || issue_s(1));
-        for (int j = 0; ok && j < n; ++j) {
-          if (j + 2 < n) {
-            ok = mbar_wait(bar(C::kBarSF + (j & 1)), (j >> 1) & 1, dead) && issue_s(j + 2);
-            if (!ok) break;
-          }
-          ok = issue_pv(j);
+        if constexpr (PAIRQ) {
+          bool ok = issue_s(0) && (n < 2 || issue_s(1));
+          for (int j = 0; ok && j < n; ++j) ok = issue_pv(j) && (j + 2 >= n || issue_s(j + 2));
+        } else {
+          bool ok = issue_s(0) && (n < 2 || issue_s(1));
+          for (int j = 0; ok && j < n; ++j) ok = (j + 2 >= n || issue_s(j + 2)) && issue_pv(j);
         }
       }
       // Every MMA this thread issued completes before the role ends.
@@ -458,21 +489,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else {
     // ------------------------------------------------------------ softmax
     // Warps 2..9: warp w reaches TMEM lanes 32 (w % 4) .. +31, so each lane
-    // quarter q has two warps, one per group (grp 0: warps 2-5, 1: 6-9). With ALT, group g owns
-    // key tiles g, g+2, ... (whole rows, its own S/P/O); otherwise both groups
-    // see every tile and own half of its key columns and half of O.
-    constexpr int SC = ALT ? BN : BN / 2;    // S columns per thread per tile
-    constexpr int OC = ALT ? HDP : HDP / 2;  // O columns this group owns
+    // quarter q has two warps, one per group (grp 0: warps 2-5, 1: 6-9).
+    constexpr int SC = SPLIT ? BN / 2 : BN;    // S columns per thread per tile
+    constexpr int OC = SPLIT ? HDP / 2 : HDP;  // O columns this group owns
     const int wq = warp & 3;
     const int grp = (warp - 2) >> 2;
     const int r = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const int s_col0 = ALT ? 0 : grp * SC;
+    const int s_col0 = SPLIT ? grp * SC : 0;
     const uint32_t o_own = C::kOCol + grp * OC;
-    const int pg = ALT ? grp : 0;
+    const int pg = SPLIT ? 0 : grp;
     const uint32_t pbuf = sP + pg * C::kPGroupBytes;
     const uint32_t xbar = bar(C::kBarX + wq);
-    const int t_local = qtile * p.QT + r / p.G;
+    const int t_local = t0 + (PAIRQ ? grp : 0) * p.QT + r / p.G;
     const bool row_valid = r < p.R && t_local < q_len;
     const int gq = q_beg + (row_valid ? t_local : 0);
     int qpos = 0, qseq = 0, qpre = -1;
@@ -490,16 +519,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int entry = list[j];
       const int kt = entry & 0x7fff;
       const bool partial = (entry & 0x8000) != 0;
-      mbar_wait(bar(C::kBarS + (j & 1)), (j >> 1) & 1, dead);
+      const int sb = PAIRQ ? grp * 2 + (j & 1) : (j & 1);
+      mbar_wait(bar(C::kBarS + sb), (j >> 1) & 1, dead);
       dead = __any_sync(0xffffffffu, dead);
       if (dead) break;
       if (warp == 4 && lane == 0) CA_EV(5, j);
       tc_fence_after();
-      // S is read from TMEM twice, LB columns at a time: pass 1 forms the row
-      // max, pass 2 exponentiates and stores P. No thread ever holds a whole
-      // 128-key row, which keeps the softmax warps within 168 registers.
-      constexpr int LB = 32;  // columns per TMEM load; chunk loops stay rolled (code size)
-      const uint32_t s_addr = tmem + lane_off + (j & 1) * BN + s_col0;
+      // S is read from TMEM twice, 32 columns at a time: pass 1 forms the row
+      // max, pass 2 exponentiates and stores P. No thread holds a whole row,
+      // which keeps the softmax warps well inside 168 registers.
+      constexpr int LB = 32;
+      const uint32_t s_addr = tmem + lane_off + sb * BN + s_col0;
       const bool fast = fast_ok && !partial;
       // Scaled log2-domain logit of column i (masked keys -> -inf); used only
       // off the fast path (partial tiles, soft-cap, negative scale).
@@ -534,9 +564,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll 1
         for (int cb = 0; cb < SC / LB; ++cb) {
           uint32_t sr[LB];
-#pragma unroll
-          for (int c = 0; c < LB / 32; ++c)
-            tmem_ld32(s_addr + cb * LB + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+          tmem_ld32(s_addr + cb * LB, sr);
           tmem_wait_ld();
           if (fast) {
 #pragma unroll
@@ -550,7 +578,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       }
       if (warp == 4 && lane == 0) CA_EV(6, j);
-      if constexpr (!ALT) {
+      if constexpr (SPLIT) {
         // Combine with the partner warp (same rows, other key columns).
         float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
         xch[((j & 1) * 2 + grp) * 128 + r] = rmax;
@@ -571,8 +599,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
 
-      // This group's P buffer and O are free once its previous P V completed
-      // (with ALT that was issued a whole group period ago).
+      // This group's P buffer and O are free once its previous P V completed.
       if (used > 0) {
         mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
         dead = __any_sync(0xffffffffu, dead);
@@ -606,7 +633,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           uint32_t sr[LB];
           tmem_ld32(s_addr + cb * LB, sr);
           tmem_wait_ld();
-          if (warp == 4 && lane == 0 && cb == 0) CA_EV(12, j);
 #pragma unroll
           for (int u = 0; u < LB / 8; ++u) {
             uint32_t pk[4], pl[4];
@@ -624,7 +650,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
             store_p(s_col0 + cb * LB + u * 8, pk, pl);
           }
-          if (warp == 4 && lane == 0 && cb == 0) CA_EV(13, j);
         }
       } else {
 #pragma unroll 1
@@ -648,7 +673,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // S[j] is fully read: its buffer may take S[j + 2].
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::kBarSF + (j & 1)));
+      if (lane == 0) mbar_arrive(bar(C::kBarSF + sb));
       l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
       if (warp == 4 && lane == 0) CA_EV(8, j);
       // Lazy correction of O (rare after the first tiles), once S is dead.
@@ -674,27 +699,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogue
-    // Wait for this group's last P V, then combine with the partner warp:
-    // ALT merges two (max, sum, O) partials; otherwise the row sums add.
+    // Wait for this group's last P V. kPairQ: the rows are the group's own.
+    // kAlt: merge the two groups' (max, sum, O) partials. kSplit: add the two
+    // halves' row sums (same running max).
     if (used > 0 && !dead) {
       mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
       dead = __any_sync(0xffffffffu, dead);
+      tc_fence_after();
     }
-    float* xo = ALT ? reinterpret_cast<float*>(smem + C::kOffP + grp * C::kPGroupBytes)
-                    : reinterpret_cast<float*>(smem + C::kOffXch) + ((n & 1) * 2 + grp) * 128;
-    float* xp = ALT ? reinterpret_cast<float*>(smem + C::kOffP + (grp ^ 1) * C::kPGroupBytes)
-                    : reinterpret_cast<float*>(smem + C::kOffXch) + ((n & 1) * 2 + (grp ^ 1)) * 128;
-    const int parity = ALT ? 0 : (n & 1);
     bool have = n > 0 && !dead;
     float s_me = 1.f, s_ot = 0.f, inv = __int_as_float(0x7fc00000);
     const int n_me = ALT ? (grp == 0 ? (n + 1) / 2 : n / 2) : n;
     const int n_ot = ALT ? (grp == 0 ? n / 2 : (n + 1) / 2) : 0;
-    if (have) {
+    if (have && PAIRQ) {
+      inv = 1.f / l;
+    } else if (have) {
+      float* xo = ALT ? reinterpret_cast<float*>(smem + C::kOffP + grp * C::kPGroupBytes)
+                      : reinterpret_cast<float*>(smem + C::kOffXch) + ((n & 1) * 2 + grp) * 128;
+      float* xp = ALT ? reinterpret_cast<float*>(smem + C::kOffP + (grp ^ 1) * C::kPGroupBytes)
+                      : reinterpret_cast<float*>(smem + C::kOffXch) + ((n & 1) * 2 + (grp ^ 1)) * 128;
       xo[r] = l;
       if (ALT) xo[128 + r] = m;
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
-      mbar_wait(xbar, parity, dead);
+      mbar_wait(xbar, ALT ? 0 : (n & 1), dead);
       dead = __any_sync(0xffffffffu, dead);
       have = !dead;
       tc_fence_after();
@@ -705,25 +733,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const float mref = mt == -INFINITY ? 0.f : mt;
         s_me = n_me > 0 ? ex2_approx(m - mref) : 0.f;
         s_ot = n_ot > 0 ? ex2_approx(m_ot - mref) : 0.f;
-        const float lt = s_me * (n_me > 0 ? l : 0.f) + s_ot * (n_ot > 0 ? l_ot : 0.f);
-        inv = 1.f / lt;
+        inv = 1.f / (s_me * (n_me > 0 ? l : 0.f) + s_ot * (n_ot > 0 ? l_ot : 0.f));
       } else {
         inv = 1.f / (l + l_ot);
       }
     }
     const int head = kvh * p.G + (r % p.G);
-    // Output columns this warp writes: with ALT group g writes columns
-    // [g HDP/2, (g+1) HDP/2) from both accumulators; otherwise its own half.
-    constexpr int WC = HDP / 2;
-    const uint32_t o_me = ALT ? C::kOCol + grp * HDP : o_own;
-    const uint32_t o_ot = C::kOCol + (grp ^ 1) * HDP;
+    // Columns this warp writes: kPairQ all of its O; kAlt half of the columns
+    // from both accumulators; kSplit its own half.
+    constexpr int WC = PAIRQ ? HDP : HDP / 2;
+    const int col0 = PAIRQ ? 0 : grp * WC;
+    const uint32_t o_me = ALT ? C::kOCol + grp * HDP + col0 : o_own;
+    const uint32_t o_ot = C::kOCol + (grp ^ 1) * HDP + col0;
 #pragma unroll 1
     for (int c = 0; c < WC / 32; ++c) {
-      const int col_base = grp * WC + c * 32;
+      const int col_base = col0 + c * 32;
       uint32_t o[32];
       float v[32];
       if (have && n_me > 0) {
-        tmem_ld32(tmem + lane_off + o_me + (ALT ? col_base : c * 32), o);
+        tmem_ld32(tmem + lane_off + o_me + c * 32, o);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = u2f(o[i]) * s_me;
@@ -732,7 +760,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
       }
       if (ALT && have && n_ot > 0) {
-        tmem_ld32(tmem + lane_off + o_ot + col_base, o);
+        tmem_ld32(tmem + lane_off + o_ot + c * 32, o);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = fmaf(u2f(o[i]), s_ot, v[i]);

@@ -89,7 +89,7 @@ struct Launch {
         return CA_ERR_CUDA;
       attr_done[dev] = true;
     }
-    const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
+    const int n_qtiles = (max_sq + C::NQ * p->QT - 1) / (C::NQ * p->QT);
     dim3 grid(n_qtiles, p->n_head_kv, p->batch);
     attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, *p);
     return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
@@ -172,16 +172,25 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
                    : 0;
 
   Launch L{a, &p, total_q, total_k, max_sq, max_sk, qrs, krs, st};
+  // One Q tile per CTA with alternating key tiles (head_dim <= 192) or split
+  // key columns (head_dim 256). The two-Q-tile mode (kPairQ, 64-key tiles)
+  // is correct but measured slower on B200 (733 vs 829 TFLOP/s at B8 S4096
+  // H16 hd128), so it is not dispatched.
+  constexpr bool pairq = false;
   if (a->precise) {
-    if (hdp == 64) return L.run<FwdCfg<64, 128, 2, true>>();
-    if (hdp == 128) return L.run<FwdCfg<128, 64, 3, true>>();
-    if (hdp == 192) return L.run<FwdCfg<192, 64, 2, true>>();
-    return L.run<FwdCfg<256, 64, 2, true>>();
+    if (hdp == 64) return pairq ? L.run<FwdCfg<64, 64, 3, true, kPairQ>>()
+                                : L.run<FwdCfg<64, 128, 2, true, kAlt>>();
+    if (hdp == 128) return pairq ? L.run<FwdCfg<128, 64, 2, true, kPairQ>>()
+                                 : L.run<FwdCfg<128, 64, 3, true, kAlt>>();
+    if (hdp == 192) return L.run<FwdCfg<192, 64, 2, true, kAlt>>();
+    return L.run<FwdCfg<256, 64, 2, true, kSplit>>();
   }
-  if (hdp == 64) return L.run<FwdCfg<64, 128, 3>>();
-  if (hdp == 128) return L.run<FwdCfg<128, 128, 2>>();
-  if (hdp == 192) return L.run<FwdCfg<192, 64, 2>>();
-  return L.run<FwdCfg<256, 64, 2>>();
+  if (hdp == 64) return pairq ? L.run<FwdCfg<64, 64, 4, false, kPairQ>>()
+                              : L.run<FwdCfg<64, 128, 3, false, kAlt>>();
+  if (hdp == 128) return pairq ? L.run<FwdCfg<128, 64, 3, false, kPairQ>>()
+                               : L.run<FwdCfg<128, 128, 2, false, kAlt>>();
+  if (hdp == 192) return L.run<FwdCfg<192, 64, 2, false, kAlt>>();
+  return L.run<FwdCfg<256, 64, 2, false, kSplit>>();
 }
 
 }  // namespace ca
