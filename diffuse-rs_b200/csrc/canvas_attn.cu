@@ -232,14 +232,15 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   pp.hd = hd;
   const long long jobs = static_cast<long long>(a->batch) * a->n_active * (H + 2 * Hkv);
   const bool vec = aligned16(a->q) && aligned16(a->k) && aligned16(a->v) &&
-                   aligned16(a->q_work) && aligned16(a->cache_k) && aligned16(a->cache_v);
+                   aligned16(a->q_work) && aligned16(a->cache_k) && aligned16(a->cache_v) &&
+                   aligned16(a->rope) && (!a->q_norm_w || aligned16(a->q_norm_w)) &&
+                   (!a->k_norm_w || aligned16(a->k_norm_w)) && a->rope_dim % 16 == 0;
   if (vec && (hd == 64 || hd == 128 || hd == 256)) {
-    const int rows_per_block = 8 * (32 / (hd / 8));
-    const int blocks = static_cast<int>(
-        std::min<long long>((jobs + rows_per_block - 1) / rows_per_block, 148LL * 32));
-    if (hd == 64) prep_block_vec_kernel<8><<<blocks, 256, 0, st>>>(pp);
-    else if (hd == 128) prep_block_vec_kernel<16><<<blocks, 256, 0, st>>>(pp);
-    else prep_block_vec_kernel<32><<<blocks, 256, 0, st>>>(pp);
+    const long long toks = static_cast<long long>(a->batch) * a->n_active;
+    const int blocks = static_cast<int>(std::min<long long>((toks + 7) / 8, 148LL * 8));
+    if (hd == 64) prep_token_kernel<8><<<blocks, 256, 0, st>>>(pp);
+    else if (hd == 128) prep_token_kernel<16><<<blocks, 256, 0, st>>>(pp);
+    else prep_token_kernel<32><<<blocks, 256, 0, st>>>(pp);
   } else {
     const int blocks = static_cast<int>(std::min<long long>((jobs + 7) / 8, 148LL * 16));
     prep_block_kernel<<<blocks, 256, 8 * hd * sizeof(float), st>>>(pp);

@@ -102,104 +102,133 @@ __global__ void __launch_bounds__(256) prep_block_kernel(const PrepParams p) {
   }
 }
 
-// Vectorised form for head_dim in {64, 128, 256}: each lane owns 8
-// consecutive elements (one 16-byte load and store), a row spans LPR =
-// head_dim / 8 lanes and a warp handles 32 / LPR rows at once. The RoPE
-// partner element (i <-> i + rope_dim/2) is read back from a per-warp staging
-// row in shared memory.
+// Vectorised form for head_dim in {64, 128, 256} with rope_dim % 16 == 0:
+// one warp per token. Each lane owns 8 consecutive elements of a row (one
+// 16-byte load and store); a row spans LPR = head_dim / 8 lanes, so a warp
+// covers 32 / LPR rows at a time and walks the token's H + 2 Hkv rows. The
+// token's RoPE (sin, cos) entries are loaded once and reused for all its Q
+// and K rows (they share the position). The partner element of the NeoX
+// rotation (i <-> i + rope_dim/2) comes from a per-warp staging row.
 template <int LPR>
-__global__ void __launch_bounds__(256) prep_block_vec_kernel(const PrepParams p) {
-  constexpr int RPW = 32 / LPR;   // rows per warp
+__global__ void __launch_bounds__(256) prep_token_kernel(const PrepParams p) {
+  constexpr int RPW = 32 / LPR;  // rows per warp per step
   constexpr int HD = LPR * 8;
-  __shared__ float stage[8][RPW][HD];
+  __shared__ __align__(16) float stage[8][RPW][HD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPR, sl = lane % LPR;
-  float* buf = stage[warp][sub];
+  const int e0 = sl * 8;
+  const int half = p.rope_dim / 2;
+  const long long n_tok = static_cast<long long>(p.batch) * p.na;
   const int per_tok = p.H + 2 * p.Hkv;
-  const long long jobs = static_cast<long long>(p.batch) * p.na * per_tok;
-  const long long wstride = static_cast<long long>(gridDim.x) * 8 * RPW;
-  for (long long base = (static_cast<long long>(blockIdx.x) * 8 + warp) * RPW; base < jobs;
-       base += wstride) {
-    const long long job = base + sub;
-    const bool active = job < jobs;
-    const long long jj = active ? job : base;
-    const long long tok = jj / per_tok;
-    const int r = static_cast<int>(jj % per_tok);
+  float* buf = stage[warp][sub];
+  for (long long tok = static_cast<long long>(blockIdx.x) * 8 + warp; tok < n_tok;
+       tok += static_cast<long long>(gridDim.x) * 8) {
+    const int pos = __ldg(p.pos + tok);
     const int b = static_cast<int>(tok / p.na);
-    const int pos = p.pos[tok];
-    const __nv_bfloat16* src;
-    __nv_bfloat16* dst;
-    const float* w = nullptr;
-    bool norm = false, rope = true;
-    if (r < p.H) {
-      src = p.q + (tok * p.H + r) * HD;
-      dst = p.q_out + (tok * p.H + r) * HD;
-      w = p.q_norm_w;
-      norm = w != nullptr;
-    } else if (r < p.H + p.Hkv) {
-      const int h = r - p.H;
-      src = p.k + (tok * p.Hkv + h) * HD;
-      dst = p.cache_k + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
-      w = p.k_norm_w;
-      norm = w != nullptr;
-    } else {
-      const int h = r - p.H - p.Hkv;
-      src = p.v + (tok * p.Hkv + h) * HD;
-      dst = p.cache_v + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
-      norm = p.v_norm != 0;
-      rope = false;
-    }
-    const int e0 = sl * 8;
-    float x[8];
+    // This lane's 8 (sin, cos) pairs: entries e0..e0+7 of the lower or upper
+    // half map to table entries (e0 mod half)..+7; rope_dim % 16 == 0 keeps
+    // them inside one half.
+    float sn[8], cs[8];
+    const bool rot = e0 < 2 * half;
     {
-      const uint4 raw = *reinterpret_cast<const uint4*>(src + e0);
-      const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+      const int idx = e0 < half ? e0 : e0 - half;
+      const float4* t4 = reinterpret_cast<const float4*>(p.rope + 2 * (static_cast<long long>(pos) * half + idx));
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        x[2 * i] = __uint_as_float(wv[i] << 16);
-        x[2 * i + 1] = __uint_as_float(wv[i] & 0xffff0000u);
+        const float4 v = rot ? __ldg(t4 + i) : make_float4(0.f, 1.f, 0.f, 1.f);
+        sn[2 * i] = v.x;
+        cs[2 * i] = v.y;
+        sn[2 * i + 1] = v.z;
+        cs[2 * i + 1] = v.w;
       }
     }
-    // Every lane of the warp joins the reductions; `norm` may differ per row.
-    double ss = 0.0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss += static_cast<double>(__fmul_rn(x[i], x[i]));
-#pragma unroll
-    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (norm) {
-      const float sc =
-          __fdiv_rn(1.f, static_cast<float>(sqrt(ss / HD + static_cast<double>(p.eps))));
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = w ? __fmul_rn(__fmul_rn(x[i], sc), w[e0 + i])
-                                           : __fmul_rn(x[i], sc);
-    }
-    const int half = rope ? p.rope_dim / 2 : 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) buf[e0 + i] = x[i];
-    __syncwarp();
-    float y[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = e0 + i;
-      if (e < half) {
-        const float2 sc2 = reinterpret_cast<const float2*>(p.rope)[static_cast<long long>(pos) * half + e];
-        y[i] = __fsub_rn(__fmul_rn(x[i], sc2.y), __fmul_rn(buf[e + half], sc2.x));
-      } else if (e < 2 * half) {
-        const int j = e - half;
-        const float2 sc2 = reinterpret_cast<const float2*>(p.rope)[static_cast<long long>(pos) * half + j];
-        y[i] = __fadd_rn(__fmul_rn(buf[j], sc2.x), __fmul_rn(x[i], sc2.y));
+    for (int r0 = 0; r0 < per_tok; r0 += RPW) {
+      const int r = r0 + sub;
+      const bool active = r < per_tok;
+      const int rr = active ? r : r0;
+      const __nv_bfloat16* src;
+      __nv_bfloat16* dst;
+      const float* w = nullptr;
+      bool norm, rope = true;
+      if (rr < p.H) {
+        src = p.q + (tok * p.H + rr) * HD;
+        dst = p.q_out + (tok * p.H + rr) * HD;
+        w = p.q_norm_w;
+        norm = w != nullptr;
+      } else if (rr < p.H + p.Hkv) {
+        const int h = rr - p.H;
+        src = p.k + (tok * p.Hkv + h) * HD;
+        dst = p.cache_k + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
+        w = p.k_norm_w;
+        norm = w != nullptr;
       } else {
-        y[i] = x[i];
+        const int h = rr - p.H - p.Hkv;
+        src = p.v + (tok * p.Hkv + h) * HD;
+        dst = p.cache_v + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
+        norm = p.v_norm != 0;
+        rope = false;  // V is not rotated (forward.rs:310 rotates Q and K only)
       }
-    }
-    __syncwarp();
-    if (active) {
-      uint4 o;
-      o.x = pack2_bf16(y[0], y[1]);
-      o.y = pack2_bf16(y[2], y[3]);
-      o.z = pack2_bf16(y[4], y[5]);
-      o.w = pack2_bf16(y[6], y[7]);
-      *reinterpret_cast<uint4*>(dst + e0) = o;
+      float x[8];
+      {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src + e0));
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x[2 * i] = __uint_as_float(wv[i] << 16);
+          x[2 * i + 1] = __uint_as_float(wv[i] & 0xffff0000u);
+        }
+      }
+      // Every lane joins the reduction; `norm` may differ between the rows.
+      double ss = 0.0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += static_cast<double>(__fmul_rn(x[i], x[i]));
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (norm) {
+        const float sc =
+            __fdiv_rn(1.f, static_cast<float>(sqrt(ss / HD + static_cast<double>(p.eps))));
+        if (w) {
+          const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + e0));
+          const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + e0) + 1);
+          const float wf[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], sc), wf[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] = __fmul_rn(x[i], sc);
+        }
+      }
+      reinterpret_cast<float4*>(buf + e0)[0] = make_float4(x[0], x[1], x[2], x[3]);
+      reinterpret_cast<float4*>(buf + e0)[1] = make_float4(x[4], x[5], x[6], x[7]);
+      __syncwarp();
+      float y[8];
+      if (rope && rot) {
+        const int pe = e0 < half ? e0 + half : e0 - half;  // partner elements
+        const float4 q0 = reinterpret_cast<const float4*>(buf + pe)[0];
+        const float4 q1 = reinterpret_cast<const float4*>(buf + pe)[1];
+        const float pr[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        if (e0 < half) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            y[i] = __fsub_rn(__fmul_rn(x[i], cs[i]), __fmul_rn(pr[i], sn[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            y[i] = __fadd_rn(__fmul_rn(pr[i], sn[i]), __fmul_rn(x[i], cs[i]));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = x[i];
+      }
+      __syncwarp();
+      if (active) {
+        uint4 o;
+        o.x = pack2_bf16(y[0], y[1]);
+        o.y = pack2_bf16(y[2], y[3]);
+        o.z = pack2_bf16(y[4], y[5]);
+        o.w = pack2_bf16(y[6], y[7]);
+        *reinterpret_cast<uint4*>(dst + e0) = o;
+      }
     }
   }
 }
