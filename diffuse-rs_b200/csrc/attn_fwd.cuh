@@ -27,6 +27,7 @@
 
 #include <climits>
 #include <cstdint>
+#include <type_traits>
 
 #include "sm100.cuh"
 
@@ -39,10 +40,13 @@ constexpr int kPolyPairs = 0;
 // Pipeline event timestamps of one CTA, compiled in only with -DCA_TRACE
 // (a diagnostic build; the product library never records them).
 #ifdef CA_TRACE
+#ifndef CA_TRACE_X
+#define CA_TRACE_X 5
+#endif
 __device__ long long g_trace[16][64];
 #define CA_EV(kind, j)                                                              \
   do {                                                                              \
-    if (blockIdx.x == 5 && blockIdx.y == 3 && blockIdx.z == 1 && (j) < 64)          \
+    if (blockIdx.x == CA_TRACE_X && blockIdx.y == 3 && blockIdx.z == 1 && (j) < 64)          \
       g_trace[kind][j] = clock64();                                                 \
   } while (0)
 #else
@@ -194,10 +198,10 @@ __device__ __forceinline__ void seq_range(const FwdParams& p, int b, int& q_beg,
   }
 }
 
-// Prologue of warps 2-3: classify every key tile of the sequence against this
-// CTA's query tile (0 = no visible pair, 1 = every pair visible, 2 = needs
-// per-element masks) and compact the visible ones into `list` (bit 15 marks
-// partial tiles). The per-tile flags are first written in place into `list`
+// Prologue of warps 0-1: classify every key tile of the sequence against this
+// CTA's query rows (0 = no visible pair, 1 = every pair visible, 2 = needs
+// per-element masks, 3 = ragged end only: every pair of its valid keys
+// visible) and compact the visible ones into `list` (kind in bits 14-15). The per-tile flags are first written in place into `list`
 // and then compacted; misc[1] receives the count.
 template <class C>
 __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_beg, int k_len,
@@ -208,7 +212,7 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
   const int n_kt = (k_len + C::BN - 1) / C::BN;
   if (!p.any_mask) {
     for (int kt = tid64; kt < n_kt; kt += 64)
-      flags[kt] = ((kt + 1) * C::BN <= k_len) ? 1 : 2;
+      flags[kt] = ((kt + 1) * C::BN <= k_len) ? 1 : 3;
   } else {
     // Query-tile summary over valid tokens.
     int* qs = misc + 4;  // [pos_min, pos_max, seq_min, seq_max, causal_min, n_causal, n_tok]
@@ -259,11 +263,11 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
           f = 0;
         } else if (all_causal && kpmin > qpmax) {
           f = 0;
-        } else if (!ragged && qsmin == qsmax && ksmin == ksmax && qsmin == ksmin &&
+        } else if (qsmin == qsmax && ksmin == ksmax && qsmin == ksmin &&
                    (p.window == kNoWindow ||
                     max(qpmax - kpmin, (long long)kpmax - qpmin) < p.window) &&
                    (!any_causal || kpmax <= cmin)) {
-          f = 1;
+          f = ragged ? 3 : 1;  // every pair visible among the tile's valid keys
         }
         flags[kt] = f;
       }
@@ -278,7 +282,9 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
       const unsigned ball = __ballot_sync(0xffffffffu, f != 0);  // all reads precede writes
       if (f) {
         const int pos = count + __popc(ball & ((1u << lane) - 1u));
-        list[pos] = static_cast<uint16_t>(kt | (f == 2 ? 0x8000 : 0));
+        // Bits 14-15: 0 every pair visible, 1 only the first (k_len - kt*BN)
+        // keys valid (ragged end, all visible), 2 per-element masks needed.
+        list[pos] = static_cast<uint16_t>(kt | (f == 2 ? 2 << 14 : f == 3 ? 1 << 14 : 0));
       }
       count += __popc(ball);
     }
@@ -387,7 +393,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int j = 0; j < n; ++j) {
         const int s = j % ST;
         if (j >= ST && !mbar_wait(bar(empty + s), ((j / ST) - 1) & 1, dead)) break;
-        const int krow = k_beg + (list[j] & 0x7fff) * BN;
+        const int krow = k_beg + (list[j] & 0x3fff) * BN;
         CA_EV(is_k ? 0 : 1, j);
         mbar_arrive_expect_tx(bar(full + s), C::kKVBytes);
 #pragma unroll
@@ -517,8 +523,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
     for (int j = ALT ? grp : 0; j < n; j += ALT ? 2 : 1) {
       const int entry = list[j];
-      const int kt = entry & 0x7fff;
-      const bool partial = (entry & 0x8000) != 0;
+      const int kt = entry & 0x3fff;
+      const int kind = entry >> 14;  // 0 full, 1 ragged end, 2 masked
+      const bool partial = kind == 2;
       const int sb = PAIRQ ? grp * 2 + (j & 1) : (j & 1);
       mbar_wait(bar(C::kBarS + sb), (j >> 1) & 1, dead);
       dead = __any_sync(0xffffffffu, dead);
@@ -530,49 +537,79 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // which keeps the softmax warps well inside 168 registers.
       constexpr int LB = 32;
       const uint32_t s_addr = tmem + lane_off + sb * BN + s_col0;
-      const bool fast = fast_ok && !partial;
-      // Scaled log2-domain logit of column i (masked keys -> -inf); used only
-      // off the fast path (partial tiles, soft-cap, negative scale).
-      auto logit = [&](uint32_t bits, int i) -> float {
-        float t;
+      // Four forms of the same arithmetic, picked per tile (uniform):
+      //   kFast     every key visible, plain scale: unrolled, FFMA + ex2
+      //   kRagged   as kFast but keys at or past `nvalid` are masked
+      //   kCapped   soft-cap (or negative scale) and no masks: unrolled
+      //   kGeneric  per-element visibility: compact rolled loop over 8-column
+      //             TMEM loads (cold: runs on a few tiles per CTA)
+      enum { kFast, kRagged, kCapped, kGeneric };
+      const int form = (partial || (kind == 1 && !fast_ok)) ? kGeneric
+                       : !fast_ok                        ? kCapped
+                       : kind == 1                       ? kRagged
+                                                         : kFast;
+      const int nvalid = kind == 1 ? k_len - kt * BN - s_col0 : SC;
+      // Scaled log2-domain logit without masks (soft-cap, any scale sign).
+      auto logit_nm = [&](uint32_t bits) -> float {
         if (p.softcap != 0.f) {
           const float x = u2f(bits) * p.scale;
-          t = p.softcap * tanh_via_exp2(x / p.softcap) * 1.4426950408889634f;
-        } else {
-          t = u2f(bits) * sl2;
+          return p.softcap * tanh_via_exp2(x / p.softcap) * 1.4426950408889634f;
         }
-        if (partial) {
-          const int kl = kt * BN + s_col0 + i;
-          bool ok = kl < k_len;
-          if (ok && p.any_mask) {
-            const int g = k_beg + kl;
-            const int kp = p.k_pos ? p.k_pos[g] : kl;
-            const int ks = p.k_seq ? p.k_seq[g] : 0;
-            ok = visible_dev(qpos, kp, qseq, ks, p.window, qpre);
-          }
-          if (!ok) t = -INFINITY;
+        return u2f(bits) * sl2;
+      };
+      // With per-element visibility (masked keys -> -inf).
+      auto logit = [&](uint32_t bits, int i) -> float {
+        float t = logit_nm(bits);
+        const int kl = kt * BN + s_col0 + i;
+        bool ok = kl < k_len;
+        if (ok && p.any_mask) {
+          const int g = k_beg + kl;
+          const int kp = p.k_pos ? p.k_pos[g] : kl;
+          const int ks = p.k_seq ? p.k_seq[g] : 0;
+          ok = visible_dev(qpos, kp, qseq, ks, p.window, qpre);
         }
-        return t;
+        return ok ? t : -INFINITY;
       };
 
       // Pass 1: row max over this thread's columns (8 independent chains).
+      // Each form is its own loop (the form is a template constant there).
       float rmax;
       {
         float mx8[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
+        auto pass1 = [&](auto form_c) {
+          constexpr int F = decltype(form_c)::value;
 #pragma unroll 1
-        for (int cb = 0; cb < SC / LB; ++cb) {
-          uint32_t sr[LB];
-          tmem_ld32(s_addr + cb * LB, sr);
-          tmem_wait_ld();
-          if (fast) {
+          for (int cb = 0; cb < SC / LB; ++cb) {
+            uint32_t sr[LB];
+            tmem_ld32(s_addr + cb * LB, sr);
+            tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < LB; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], u2f(sr[i]));
-          } else {
-#pragma unroll
-            for (int i = 0; i < LB; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], logit(sr[i], cb * LB + i));
+            for (int i = 0; i < LB; ++i) {
+              float v;
+              if constexpr (F == kFast) v = u2f(sr[i]);
+              else if constexpr (F == kRagged) v = cb * LB + i < nvalid ? u2f(sr[i]) : -INFINITY;
+              else v = logit_nm(sr[i]);
+              mx8[i & 7] = fmaxf(mx8[i & 7], v);
+            }
           }
+        };
+        if (form == kGeneric) {
+#pragma unroll 1
+          for (int c8 = 0; c8 < SC / 8; ++c8) {
+            uint32_t sr[8];
+            tmem_ld8(s_addr + c8 * 8, sr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(mx8[i], logit(sr[i], c8 * 8 + i));
+          }
+        } else if (form == kFast) {
+          pass1(std::integral_constant<int, kFast>{});
+        } else if (form == kRagged) {
+          pass1(std::integral_constant<int, kRagged>{});
+        } else {
+          pass1(std::integral_constant<int, kCapped>{});
         }
         rmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
@@ -589,7 +626,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (dead) break;
         rmax = fmaxf(rmax, xch[((j & 1) * 2 + (grp ^ 1)) * 128 + r]);
       }
-      const float mcand = fast ? rmax * sl2 : rmax;
+      // kFast / kRagged maxima are raw scores; the others are already scaled.
+      const bool raw = form == kFast || form == kRagged;
+      const float mcand = raw ? rmax * sl2 : rmax;
 
       const bool resc = mcand > m + 8.f;
       float corr = 1.f;
@@ -609,8 +648,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (warp == 4 && lane == 0) CA_EV(7, j);
       // Pass 2: exponentiate 8 keys at a time and store them straight into P
       // (row r: 128-byte rows of 64 keys, 16-byte units XOR-swizzled by r & 7).
-      // The fast and the masked/soft-capped forms are separate loops so the
-      // hot one carries no code of the other.
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
       auto store_p = [&](int key0, const uint32_t (&pk)[4], const uint32_t (&pl)[4]) {
         const uint32_t addr =
@@ -627,48 +664,59 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           pl[q2] = pack_bf16(p0 - h0, p1 - h1);
         }
       };
-      if (fast) {
+      if (form == kGeneric) {
 #pragma unroll 1
-        for (int cb = 0; cb < SC / LB; ++cb) {
-          uint32_t sr[LB];
-          tmem_ld32(s_addr + cb * LB, sr);
+        for (int c8 = 0; c8 < SC / 8; ++c8) {
+          uint32_t sr[8], pk[4], pl[4];
+          tmem_ld8(s_addr + c8 * 8, sr);
           tmem_wait_ld();
 #pragma unroll
-          for (int u = 0; u < LB / 8; ++u) {
-            uint32_t pk[4], pl[4];
-#pragma unroll
-            for (int q2 = 0; q2 < 4; ++q2) {
-              const int i = u * 8 + q2 * 2;
-              // Pairs selected by kPolyPairs go through the FMA-pipe exp2
-              // (ex2_poly); measured break-even is low, so it is off.
-              const float x0 = fmaf(u2f(sr[i]), sl2, -mu);
-              const float x1 = fmaf(u2f(sr[i + 1]), sl2, -mu);
-              if ((kPolyPairs >> q2) & 1)
-                emit(ex2_poly(x0), ex2_poly(x1), q2, pk, pl);
-              else
-                emit(ex2_approx(x0), ex2_approx(x1), q2, pk, pl);
-            }
-            store_p(s_col0 + cb * LB + u * 8, pk, pl);
-          }
+          for (int q2 = 0; q2 < 4; ++q2)
+            emit(ex2_approx(logit(sr[2 * q2], c8 * 8 + 2 * q2) - mu),
+                 ex2_approx(logit(sr[2 * q2 + 1], c8 * 8 + 2 * q2 + 1) - mu), q2, pk, pl);
+          store_p(s_col0 + c8 * 8, pk, pl);
         }
       } else {
+        auto pass2 = [&](auto form_c) {
+          constexpr int F = decltype(form_c)::value;
 #pragma unroll 1
-        for (int cb = 0; cb < SC / LB; ++cb) {
-          uint32_t sr[LB];
-          tmem_ld32(s_addr + cb * LB, sr);
-          tmem_wait_ld();
+          for (int cb = 0; cb < SC / LB; ++cb) {
+            uint32_t sr[LB];
+            tmem_ld32(s_addr + cb * LB, sr);
+            tmem_wait_ld();
 #pragma unroll
-          for (int u = 0; u < LB / 8; ++u) {
-            uint32_t pk[4], pl[4];
+            for (int u = 0; u < LB / 8; ++u) {
+              uint32_t pk[4], pl[4];
 #pragma unroll
-            for (int q2 = 0; q2 < 4; ++q2) {
-              const int i = u * 8 + q2 * 2;
-              emit(ex2_approx(logit(sr[i], cb * LB + i) - mu),
-                   ex2_approx(logit(sr[i + 1], cb * LB + i + 1) - mu), q2, pk, pl);
+              for (int q2 = 0; q2 < 4; ++q2) {
+                const int i = u * 8 + q2 * 2;
+                float x0, x1;
+                if constexpr (F == kCapped) {
+                  x0 = logit_nm(sr[i]) - mu;
+                  x1 = logit_nm(sr[i + 1]) - mu;
+                } else {
+                  x0 = fmaf(u2f(sr[i]), sl2, -mu);
+                  x1 = fmaf(u2f(sr[i + 1]), sl2, -mu);
+                  if constexpr (F == kRagged) {
+                    x0 = cb * LB + i < nvalid ? x0 : -INFINITY;
+                    x1 = cb * LB + i + 1 < nvalid ? x1 : -INFINITY;
+                  }
+                }
+                // Pairs selected by kPolyPairs go through the FMA-pipe exp2
+                // (ex2_poly, never given -inf); measured break-even is low,
+                // so it is off.
+                if (F == kFast && ((kPolyPairs >> q2) & 1))
+                  emit(ex2_poly(x0), ex2_poly(x1), q2, pk, pl);
+                else
+                  emit(ex2_approx(x0), ex2_approx(x1), q2, pk, pl);
+              }
+              store_p(s_col0 + cb * LB + u * 8, pk, pl);
             }
-            store_p(s_col0 + cb * LB + u * 8, pk, pl);
           }
-        }
+        };
+        if (form == kFast) pass2(std::integral_constant<int, kFast>{});
+        else if (form == kRagged) pass2(std::integral_constant<int, kRagged>{});
+        else pass2(std::integral_constant<int, kCapped>{});
       }
       // S[j] is fully read: its buffer may take S[j + 2].
       tc_fence_before();
