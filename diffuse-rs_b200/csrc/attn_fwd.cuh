@@ -168,10 +168,11 @@ __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
 
 // tanh(x) = 1 - 2 / (e^{2x} + 1), with e^{2x} = 2^{2x log2 e}; |x| clamped at
-// 15 where tanh is 1 to fp32 precision. Used only by the soft-cap extension.
+// 15 where tanh is 1 to fp32 precision. Used only by the soft-cap extension;
+// the exponential runs on the FMA pipe (ex2_poly) to spare the MUFU unit.
 __device__ __forceinline__ float tanh_via_exp2(float x) {
   x = fminf(fmaxf(x, -15.f), 15.f);
-  const float e = ex2_approx(x * 2.8853900817779268f);  // 2 * log2(e)
+  const float e = ex2_poly(x * 2.8853900817779268f);  // 2 * log2(e)
   return 1.f - __fdividef(2.f, e + 1.f);
 }
 
@@ -518,6 +519,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     const float sl2 = p.scale_log2;
     const bool fast_ok = p.softcap == 0.f && sl2 >= 0.f;
+    // Soft-cap: logit = cap * tanh(score * scale / cap), in log2 units.
+    const float scale_cap = p.softcap != 0.f ? p.scale / p.softcap : 0.f;
+    const float cap_l2 = p.softcap * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
     int used = 0;  // tiles this thread has processed
 
@@ -549,12 +553,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                        : kind == 1                       ? kRagged
                                                          : kFast;
       const int nvalid = kind == 1 ? k_len - kt * BN - s_col0 : SC;
+      const float sgn = p.scale < 0.f ? -1.f : 1.f;
       // Scaled log2-domain logit without masks (soft-cap, any scale sign).
       auto logit_nm = [&](uint32_t bits) -> float {
-        if (p.softcap != 0.f) {
-          const float x = u2f(bits) * p.scale;
-          return p.softcap * tanh_via_exp2(x / p.softcap) * 1.4426950408889634f;
-        }
+        if (p.softcap != 0.f) return cap_l2 * tanh_via_exp2(u2f(bits) * scale_cap);
         return u2f(bits) * sl2;
       };
       // With per-element visibility (masked keys -> -inf).
@@ -590,7 +592,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               float v;
               if constexpr (F == kFast) v = u2f(sr[i]);
               else if constexpr (F == kRagged) v = cb * LB + i < nvalid ? u2f(sr[i]) : -INFINITY;
-              else v = logit_nm(sr[i]);
+              else v = sgn * u2f(sr[i]);  // kCapped: logit is monotonic in the raw score
               mx8[i & 7] = fmaxf(mx8[i & 7], v);
             }
           }
@@ -626,9 +628,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (dead) break;
         rmax = fmaxf(rmax, xch[((j & 1) * 2 + (grp ^ 1)) * 128 + r]);
       }
-      // kFast / kRagged maxima are raw scores; the others are already scaled.
-      const bool raw = form == kFast || form == kRagged;
-      const float mcand = raw ? rmax * sl2 : rmax;
+      // kFast / kRagged maxima are raw scores; kCapped's is sgn * raw score
+      // (the soft-capped logit is monotonic in it); kGeneric's is a logit.
+      float mcand;
+      if (form == kFast || form == kRagged) mcand = rmax * sl2;
+      else if (form == kCapped) mcand = rmax == -INFINITY ? rmax : logit_nm(f2u(sgn * rmax));
+      else mcand = rmax;
 
       const bool resc = mcand > m + 8.f;
       float corr = 1.f;
