@@ -30,12 +30,15 @@ CA_ERR_UNSUPPORTED = -2
 CA_ERR_CUDA = -3
 CA_ERR_TIMEOUT = -4
 CA_ERR_NOMEM = -5
+CA_ERR_SCRATCH = -6
+NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
 
 # Every symbol include/canvas_attn.h declares.
 EXPORTED_SYMBOLS = (
     "ca_attention_host_f32",
     "ca_attention_dev",
     "ca_attention_block_dev",
+    "ca_attention_block_dev_noalloc",
     "ca_build_rope_table",
     "ca_device_status",
     "ca_status_string",
@@ -107,6 +110,8 @@ def _load():
     L.ca_attention_dev.restype = ctypes.c_int
     L.ca_attention_block_dev.argtypes = [ctypes.POINTER(CaBlockArgs), ctypes.c_void_p]
     L.ca_attention_block_dev.restype = ctypes.c_int
+    L.ca_attention_block_dev_noalloc.argtypes = [ctypes.POINTER(CaBlockArgs), ctypes.c_void_p]
+    L.ca_attention_block_dev_noalloc.restype = ctypes.c_int
     L.ca_build_rope_table.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                       ctypes.c_float, ctypes.c_void_p]
     L.ca_build_rope_table.restype = ctypes.c_int
@@ -264,6 +269,17 @@ def attention_block_dev(*args, stream=None, **kw) -> None:
     a = make_block_args(*args, **kw)
     _check(lib.ca_attention_block_dev(ctypes.byref(a), _stream(stream)),
            "ca_attention_block_dev")
+
+
+def attention_block_dev_noalloc(*args, stream=None, **kw) -> None:
+    """ca_attention_block_dev_noalloc: the fused block for callers that cannot
+    allocate device memory; pass q_work=None (the library's fixed 16 MiB
+    scratch holds the rotated queries). Overlapping calls race on that
+    scratch; the first call on a device should precede any stream capture."""
+    kw.setdefault("q_work", None)
+    a = make_block_args(*args, **kw)
+    _check(lib.ca_attention_block_dev_noalloc(ctypes.byref(a), _stream(stream)),
+           "ca_attention_block_dev_noalloc")
 
 
 def build_rope_cache(max_seq_len: int, rope_dim: int, theta: float,

@@ -431,7 +431,54 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
 }  // namespace
 }  // namespace ca
 
+namespace ca {
+namespace {
+
+// Scratch of ca_attention_block_dev_noalloc: the post-norm, post-RoPE Q of
+// one call. In host code this name is only a stand-in for the per-device
+// copy; its device address comes from cudaGetSymbolAddress below.
+constexpr size_t kNoAllocElems = CA_NOALLOC_SCRATCH_BYTES / sizeof(__nv_bfloat16);
+static __device__ __align__(256) __nv_bfloat16 g_noalloc_qwork[kNoAllocElems];
+
+struct NoAllocSlot {
+  std::once_flag once;
+  void* ptr = nullptr;
+  int rc = CA_ERR_CUDA;
+};
+NoAllocSlot g_noalloc[kMaxDevices];
+
+int noalloc_impl(const ca_block_args* a, cudaStream_t st) {
+  if (!a) return CA_ERR_INVALID;
+  if (a->q_work) return CA_ERR_INVALID;  // the library supplies the scratch
+  if (a->batch < 0 || a->n_active < 0 || a->n_head <= 0 || a->head_dim <= 0)
+    return CA_ERR_INVALID;
+  const unsigned long long need = static_cast<unsigned long long>(a->batch) * a->n_active *
+                                  a->n_head * a->head_dim;
+  if (need > kNoAllocElems) return CA_ERR_SCRATCH;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
+  NoAllocSlot& slot = g_noalloc[dev];
+  std::call_once(slot.once, [&slot] {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_qwork) == cudaSuccess && ptr) {
+      slot.ptr = ptr;
+      slot.rc = CA_OK;
+    }
+  });
+  if (slot.rc != CA_OK) return slot.rc;
+  ca_block_args b = *a;
+  b.q_work = slot.ptr;
+  return block_impl(&b, st);
+}
+
+}  // namespace
+}  // namespace ca
+
 extern "C" {
+
+int ca_attention_block_dev_noalloc(const ca_block_args* a, void* stream) {
+  return ca::noalloc_impl(a, static_cast<cudaStream_t>(stream));
+}
 
 int ca_attention_host_f32(float* out, const float* q, const float* k, const float* v,
                           const ca_shape* s, const ca_rows* qr, const ca_rows* kr) {
@@ -486,6 +533,7 @@ const char* ca_status_string(int status) {
     case CA_ERR_CUDA: return "CUDA error";
     case CA_ERR_TIMEOUT: return "device-side wait timed out";
     case CA_ERR_NOMEM: return "out of memory";
+    case CA_ERR_SCRATCH: return "request exceeds the no-allocation entry point's fixed scratch";
     default: return "unknown status";
   }
 }

@@ -30,7 +30,9 @@ typedef enum {
     CA_ERR_UNSUPPORTED = -2, /* valid for the reference, not for this build (e.g. head_dim > 256) */
     CA_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed */
     CA_ERR_TIMEOUT = -4,     /* a bounded device-side wait expired; outputs are undefined */
-    CA_ERR_NOMEM = -5        /* device or pinned allocation failed */
+    CA_ERR_NOMEM = -5,       /* device or pinned allocation failed */
+    CA_ERR_SCRATCH = -6      /* request larger than the fixed scratch of
+                                ca_attention_block_dev_noalloc */
 } ca_status;
 
 /* Mirrors AttnShape (src/model/attention.rs:10-27). Option<usize> fields use
@@ -169,6 +171,29 @@ typedef struct {
  * Asynchronous on `stream`; allocates nothing.
  */
 int ca_attention_block_dev(const ca_block_args* a, void* stream);
+
+/*
+ * ca_attention_block_dev_noalloc -- no counterpart in the reference. The
+ * same fused block as ca_attention_block_dev for callers that cannot allocate
+ * device memory themselves: hosts that link only this library and hold no
+ * CUDA allocator, or programs whose framework owns every device allocation
+ * and forbids extra cudaMalloc calls. The caller passes inputs, cache and
+ * output as usual but leaves a->q_work NULL: the normed, rotated queries go to
+ * a scratch array compiled into the library (static device memory of
+ * CA_NOALLOC_SCRATCH_BYTES = 16 MiB on every GPU that loads the library,
+ * held until process exit). Requests needing more than that
+ * (batch * n_active * n_head * head_dim * 2 bytes > 16 MiB) return
+ * CA_ERR_SCRATCH before anything is launched. Nothing is allocated: no
+ * cudaMalloc, no cudaFree, no allocating library call.
+ * The first call on a device looks up the scratch array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture. All calls share the one array, so calls whose
+ * GPU work overlaps (other streams, other threads) race on it; the scratch
+ * keeps the last call's values, which is harmless because every call writes
+ * all of the scratch it reads before reading it.
+ */
+int ca_attention_block_dev_noalloc(const ca_block_args* a, void* stream);
+#define CA_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
 /*
  * ca_build_rope_table -- replaces build_rope_cache_ff (src/model/ops.rs:398-416),
