@@ -297,8 +297,12 @@ class CpuSample:
     def calibrate(self, target_s):
         n = 64 * len(self.cfg["layers"])
         self.run(n)  # thread-pool start-up
-        f, s = self.run(4 * n)
-        return max(16, int(4 * n / max(s, 1e-6) * target_s))
+        for _ in range(3):  # grow the probe until it takes ~0.5 s
+            f, s = self.run(n)
+            if s > 0.5:
+                break
+            n = int(n * min(16.0, 0.6 / max(s, 1e-4)))
+        return max(16, int(n / max(s, 1e-6) * target_s))
 
     def describe(self, n_rows, config):
         return (f"{n_rows} (head, query) rows of one {config} sequence spread over "

@@ -237,7 +237,8 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
                    (!a->k_norm_w || aligned16(a->k_norm_w)) && a->rope_dim % 16 == 0;
   if (vec && (hd == 64 || hd == 128 || hd == 256)) {
     const long long toks = static_cast<long long>(a->batch) * a->n_active;
-    const int blocks = static_cast<int>(std::min<long long>((toks + 7) / 8, 148LL * 8));
+    const long long pjobs = toks * ((H + 2 * Hkv + 15) / 16);
+    const int blocks = static_cast<int>(std::min<long long>((pjobs + 7) / 8, 148LL * 8));
     if (hd == 64) prep_token_kernel<8><<<blocks, 256, 0, st>>>(pp);
     else if (hd == 128) prep_token_kernel<16><<<blocks, 256, 0, st>>>(pp);
     else prep_token_kernel<32><<<blocks, 256, 0, st>>>(pp);

@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(256) prep_block_kernel(const PrepParams p) {
 }
 
 // Vectorised form for head_dim in {64, 128, 256} with rope_dim % 16 == 0:
-// one warp per token. Each lane owns 8 consecutive elements of a row (one
+// one warp per (token, group of up to 16 rows). Each lane owns 8 consecutive elements of a row (one
 // 16-byte load and store); a row spans LPR = head_dim / 8 lanes, so a warp
 // covers 32 / LPR rows at a time and walks the token's H + 2 Hkv rows. The
 // token's RoPE (sin, cos) entries are loaded once and reused for all its Q
@@ -120,9 +120,17 @@ __global__ void __launch_bounds__(256) prep_token_kernel(const PrepParams p) {
   const int half = p.rope_dim / 2;
   const long long n_tok = static_cast<long long>(p.batch) * p.na;
   const int per_tok = p.H + 2 * p.Hkv;
+  // A job is up to kRowsPerJob rows of one token, so small batches still
+  // spread over many warps.
+  constexpr int kRowsPerJob = 16;
+  const int chunks = (per_tok + kRowsPerJob - 1) / kRowsPerJob;
+  const long long n_jobs = n_tok * chunks;
   float* buf = stage[warp][sub];
-  for (long long tok = static_cast<long long>(blockIdx.x) * 8 + warp; tok < n_tok;
-       tok += static_cast<long long>(gridDim.x) * 8) {
+  for (long long job = static_cast<long long>(blockIdx.x) * 8 + warp; job < n_jobs;
+       job += static_cast<long long>(gridDim.x) * 8) {
+    const long long tok = job / chunks;
+    const int row_beg = static_cast<int>(job % chunks) * kRowsPerJob;
+    const int row_end = min(per_tok, row_beg + kRowsPerJob);
     const int pos = __ldg(p.pos + tok);
     const int b = static_cast<int>(tok / p.na);
     // This lane's 8 (sin, cos) pairs: entries e0..e0+7 of the lower or upper
@@ -142,9 +150,9 @@ __global__ void __launch_bounds__(256) prep_token_kernel(const PrepParams p) {
         cs[2 * i + 1] = v.w;
       }
     }
-    for (int r0 = 0; r0 < per_tok; r0 += RPW) {
+    for (int r0 = row_beg; r0 < row_end; r0 += RPW) {
       const int r = r0 + sub;
-      const bool active = r < per_tok;
+      const bool active = r < row_end;
       const int rr = active ? r : r0;
       const __nv_bfloat16* src;
       __nv_bfloat16* dst;
