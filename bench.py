@@ -265,7 +265,12 @@ class CpuSample:
         self.v = rnd(nk * c["Hkv"] * c["hd"])
         self.q_pos = np.arange(c["start"], c["start"] + c["na"], dtype=np.int64)
         self.k_pos = np.arange(nk, dtype=np.int64)
-        self.threads = orc.max_threads()
+        # All host threads, whatever OMP_NUM_THREADS a launcher (torchrun
+        # sets 1) put in the environment.
+        try:
+            self.threads = len(os.sched_getaffinity(0))
+        except AttributeError:
+            self.threads = os.cpu_count() or orc.max_threads()
         self.kind = orc.ROW_AVX2 if orc.have_avx2() else orc.ROW_SCALAR
         self.out = np.zeros(c["na"] * c["H"] * c["hd"], dtype=np.float32)
 
