@@ -15,14 +15,17 @@
 //   warps 2-9   softmax, O correction and epilogue in two groups of four
 //               warps (2-5 and 6-9); warp w reaches TMEM lanes 32 (w % 4)..+31
 //
-// Pipeline per visible key tile j (S double-buffered in TMEM, P in smem):
+// Pipeline per visible key tile j (S double-buffered in TMEM; P in TMEM too):
 //   S[j&1] = Q K_j^T           (tcgen05.mma, SS, fp32 accumulate in TMEM)
-//   P_j    = exp2(S*c - m)     (softmax warps, bf16 into swizzled smem)
-//   O     += P_j V_j           (tcgen05.mma, SS, V read MN-major)
-// The MMA warp issues S[j+1] before PV[j], so the tensor core works on the
-// next tile while the softmax warps exponentiate this one. Running maxima are
-// rescaled lazily: O is corrected only when a row max grows by more than 2^8,
-// which is exact (the final 1/l uses the same stale max).
+//   P_j    = exp2(S*c - m)     (softmax warps, bf16 written over S[j&1])
+//   O     += P_j V_j           (tcgen05.mma, TS: P from TMEM, V MN-major smem)
+// Keeping P out of shared memory matters: while SS MMAs stream their operands
+// at N = 128, ordinary shared-memory stores from other warps barely progress.
+// Two softmax groups take alternate key tiles (or, head_dim 256, halves of
+// each tile), so one group exponentiates while the tensor core runs the other
+// group's MMAs. Running maxima are rescaled lazily: O is corrected only when a
+// row max grows by more than 2^8, which is exact (the final 1/l uses the same
+// stale max).
 #pragma once
 
 #include <climits>
@@ -34,8 +37,6 @@
 namespace ca {
 
 constexpr int kNoWindow = INT_MAX;
-// Bit q of kPolyPairs: pair q of every 8 keys uses the FMA-pipe exp2.
-constexpr int kPolyPairs = 0;
 
 // Pipeline event timestamps of one CTA, compiled in only with -DCA_TRACE
 // (a diagnostic build; the product library never records them).
@@ -80,65 +81,59 @@ struct FwdParams {
 };
 
 // Softmax organisation of a CTA (see the file comment):
-//   kSplit  one Q tile; both warp groups see every key tile, each on half of
-//           its key columns and half of O (head_dim 256: TMEM holds one O)
-//   kAlt    one Q tile; group g takes key tiles g, g+2, ... with its own S, P
-//           and O, merged at the end (head_dim 192, or a single Q tile)
-//   kPairQ  two Q tiles sharing every K/V tile; group g owns Q tile g with a
-//           double-buffered S, its own P and O (head_dim <= 128)
-enum FwdMode { kSplit = 0, kAlt = 1, kPairQ = 2 };
+//   kSplit  both warp groups see every key tile, each on half of its key
+//           columns and half of O (head_dim 256: TMEM holds one O)
+//   kAlt    group g takes key tiles g, g+2, ... with its own S/P buffer and
+//           O, merged at the end (head_dim <= 192)
+enum FwdMode { kSplit = 0, kAlt = 1 };
 
-template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_>
+
+template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_, int SB_ = (MODE_ == 0 ? 3 : 2)>
 struct FwdCfg {
   static constexpr int HDP = HDP_;  // head_dim padded to a multiple of 64
   static constexpr int BN = BN_;    // keys per tile
   static constexpr int ST = ST_;    // stages of each of the K and V rings
-  // PRECISE: P is split into bf16 hi + lo terms (two PV MMAs), so the softmax
-  // weights reach the tensor core with ~16 significant bits instead of 8.
+  // PRECISE: P is split into bf16 hi + lo terms (two P V MMAs), so the
+  // softmax weights reach the tensor core with ~16 significant bits, not 8.
   static constexpr bool PRECISE = PRECISE_;
   static constexpr int MODE = MODE_;
   static constexpr bool ALT = MODE == kAlt;
-  static constexpr bool PAIRQ = MODE == kPairQ;
   static constexpr bool SPLIT = MODE == kSplit;
   static constexpr int kPTerms = PRECISE ? 2 : 1;
-  static constexpr int NQ = PAIRQ ? 2 : 1;       // Q tiles per CTA
-  static constexpr int kGroupsP = SPLIT ? 1 : 2;  // P buffers / O accumulators
-  static constexpr int SB = PAIRQ ? 4 : 2;       // S buffers in TMEM
+  // S buffers in TMEM (P overwrites S in place). kSplit keeps one O, which
+  // leaves room for a third buffer: S runs two tiles ahead of the softmax.
+  // kAlt with 64-key tiles fits four: each group double-buffers its S.
+  static constexpr int SB = SB_;
+  static_assert(SPLIT ? SB == 3 : (SB == 2 || SB == 4), "S buffering");
   static constexpr int kChunks = HDP / 64;  // 128-byte swizzle atoms along head_dim
   static constexpr int kQChunk = 128 * 128;
   static constexpr int kKChunk = BN * 128;
-  static constexpr int kPChunk = 128 * 128;
-  static constexpr int kQBytes = kChunks * kQChunk;  // one Q tile
+  static constexpr int kQBytes = kChunks * kQChunk;
   static constexpr int kKVBytes = kChunks * kKChunk;
-  static constexpr int kPTermBytes = (BN / 64) * kPChunk;
-  static constexpr int kPGroupBytes = kPTerms * kPTermBytes;
-  static constexpr int kPBytes = kGroupsP * kPGroupBytes;
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + NQ * kQBytes;
+  static constexpr int kOffK = kOffQ + kQBytes;
   static constexpr int kOffV = kOffK + ST * kKVBytes;
-  static constexpr int kOffP = kOffV + ST * kKVBytes;
-  static constexpr int kOffBar = kOffP + kPBytes;
+  static constexpr int kOffBar = kOffV + ST * kKVBytes;
   // Barriers. K and V stages are released separately: a K stage as soon as
-  // its Q K^T MMA(s) complete, a V stage when its P V MMA(s) complete.
+  // its Q K^T MMA completes, a V stage when its P V MMA(s) complete.
   static constexpr int kBarQ = 0;
   static constexpr int kBarK = 1;             // [ST] K tile landed
   static constexpr int kBarV = kBarK + ST;    // [ST] V tile landed
   static constexpr int kBarKE = kBarV + ST;   // [ST] K stage free
   static constexpr int kBarVE = kBarKE + ST;  // [ST] V stage free
   static constexpr int kBarS = kBarVE + ST;   // [SB] S buffer holds Q K^T
-  static constexpr int kBarSF = kBarS + SB;   // [SB] S buffer read out by softmax
-  static constexpr int kBarP = kBarSF + SB;   // [2] P written (per P buffer)
+  static constexpr int kBarP = kBarS + SB;    // [2] P written over S (per group)
   static constexpr int kBarO = kBarP + 2;     // [2] P V done (per O accumulator)
   static constexpr int kBarF = kBarO + 2;     // all MMAs done
   static constexpr int kBarX = kBarF + 1;     // [4] softmax warp-pair exchange
   static constexpr int kNumBars = kBarX + 4;
   // Largest key-tile count per sequence (keys <= kMaxTiles * BN).
-  static constexpr int kMaxTiles = (PRECISE && HDP == 256) ? 256 : 1024;
+  static constexpr int kMaxTiles = 1024;
   static constexpr int kOffList = kOffBar + kNumBars * 8;
-  // Warp-pair exchange, float [parity][half][128]. Outside kSplit it is used
-  // once, after the last P V, and lives in the then idle P buffers.
+  // Warp-pair exchange, float [parity][half][128]. kAlt uses it once, after
+  // the last P V, in the then idle K ring; kSplit every tile, in its own area.
   static constexpr int kXchBytes = 2 * 2 * 128 * 4;
-  static constexpr int kOffXch = SPLIT ? kOffList + kMaxTiles * 2 : kOffP;
+  static constexpr int kOffXch = SPLIT ? kOffList + kMaxTiles * 2 : kOffK;
   static constexpr int kOffMisc = kOffList + kMaxTiles * 2 + (SPLIT ? kXchBytes : 0);
   static constexpr int kMiscBytes = 64;
   static constexpr int kSmemBytes = kOffMisc + kMiscBytes;
@@ -147,7 +142,7 @@ struct FwdCfg {
   static constexpr uint32_t kIdescS = umma_idesc_bf16(128, BN, 0, 0);
   static constexpr uint32_t kIdescO = umma_idesc_bf16(128, HDP, 0, 1);
   static_assert(kOCol + (SPLIT ? 1 : 2) * HDP <= kTmemCols, "TMEM budget");
-  static_assert(SPLIT || kPBytes >= kXchBytes, "exchange fits in the P buffers");
+  static_assert(SPLIT || ST * kKVBytes >= kXchBytes, "exchange fits in the K ring");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 256, "tile shape");
 };
@@ -302,8 +297,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
-  constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST, NQ = C::NQ;
-  constexpr bool ALT = C::ALT, PAIRQ = C::PAIRQ, SPLIT = C::SPLIT;
+  constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST;
+  constexpr bool ALT = C::ALT, SPLIT = C::SPLIT;
   // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
   // static shared memory, so the dynamic window starts 1024-aligned; if it
   // ever did not, report it instead of computing garbage.
@@ -315,19 +310,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int qtile = blockIdx.x;  // index of this CTA's group of NQ query tiles
+  const int qtile = blockIdx.x;  // query tile
   const int kvh = blockIdx.y;
   const int b = blockIdx.z;
 
   int q_beg, q_len, k_beg, k_len;
   seq_range(p, b, q_beg, q_len, k_beg, k_len);
-  const int t0 = qtile * NQ * p.QT;  // first query token of this CTA
+  const int t0 = qtile * p.QT;  // first query token of this CTA
   if (t0 >= q_len) return;           // uniform across the CTA
 
   const uint32_t sQ = smem_u32(smem + C::kOffQ);
   const uint32_t sK = smem_u32(smem + C::kOffK);
   const uint32_t sV = smem_u32(smem + C::kOffV);
-  const uint32_t sP = smem_u32(smem + C::kOffP);
   const uint32_t bar0 = smem_u32(smem + C::kOffBar);
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * i; };
   uint16_t* list = reinterpret_cast<uint16_t*>(smem + C::kOffList);
@@ -341,10 +335,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(bar(C::kBarKE + s), 1);
       mbar_init(bar(C::kBarVE + s), 1);
     }
-    for (int i = 0; i < C::SB; ++i) {
-      mbar_init(bar(C::kBarS + i), 1);
-      mbar_init(bar(C::kBarSF + i), SPLIT ? 8 : 4);
-    }
+    for (int i = 0; i < C::SB; ++i) mbar_init(bar(C::kBarS + i), 1);
     for (int g = 0; g < 2; ++g) {
       mbar_init(bar(C::kBarP + g), SPLIT ? 8 : 4);
       mbar_init(bar(C::kBarO + g), 1);
@@ -364,7 +355,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tmem_relinquish();
   }
   if (warp <= 1)
-    build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, t0, NQ * p.QT, list, misc, tid);
+    build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, t0, p.QT, list, misc, tid);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -383,13 +374,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int full = is_k ? C::kBarK : C::kBarV;
       const int empty = is_k ? C::kBarKE : C::kBarVE;
       if (is_k) {
-        mbar_arrive_expect_tx(bar(C::kBarQ), NQ * C::kChunks * 128u * p.R);
+        mbar_arrive_expect_tx(bar(C::kBarQ), C::kChunks * 128u * p.R);
 #pragma unroll
-        for (int t = 0; t < NQ; ++t)
-#pragma unroll
-          for (int c = 0; c < C::kChunks; ++c)
-            tma_load_3d(sQ + t * C::kQBytes + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64,
-                        kvh * p.G, q_beg + t0 + t * p.QT);
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(sQ + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64, kvh * p.G, q_beg + t0);
       }
       for (int j = 0; j < n; ++j) {
         const int s = j % ST;
@@ -410,83 +398,82 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      // S buffer of (tile j, Q tile g), and how often it was used before.
-      auto sbuf = [&](int j, int g) -> int { return PAIRQ ? g * 2 + (j & 1) : (j & 1); };
-      // Q K^T of tile j for Q tile g (waits for the buffer's previous reader).
-      auto mma_s = [&](int j, int g, uint32_t kbase) -> bool {
-        const int sb = sbuf(j, g);
-        if (j >= 2 && !mbar_wait(bar(C::kBarSF + sb), ((j - 2) >> 1) & 1, dead)) return false;
+      // The P V accumulator tile i goes into, and its use count.
+      auto og = [&](int i) -> int { return ALT ? (i & 1) : 0; };
+      auto ouse = [&](int i) -> int { return ALT ? (i >> 1) : i; };
+      // S[j] = Q K_j^T into S buffer j % SB. That buffer last held P[j - SB],
+      // so P V[j - SB] must have completed (it reads P from there). kAlt
+      // waits for it here (no later P V on that barrier is issued yet);
+      // kSplit issues S[j] after P V[j - 2], whose issue already waited for
+      // P V[j - 3].
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % ST;
+        const int sb = j % C::SB;
+        if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) return false;
+#ifndef CA_INORDER
+        if (ALT && j >= C::SB &&
+            !mbar_wait(bar(C::kBarO + og(j - C::SB)), ouse(j - C::SB) & 1, dead))
+          return false;
+#else
+        if (ALT && C::SB > 2 && j >= C::SB &&
+            !mbar_wait(bar(C::kBarO + og(j - C::SB)), ouse(j - C::SB) & 1, dead))
+          return false;
+#endif
+        CA_EV(2, j);
         tc_fence_after();
-        const uint32_t qbase = sQ + g * C::kQBytes;
+        const uint32_t kbase = sK + s * C::kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < HDP / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(qbase + (kk >> 2) * C::kQChunk + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = umma_desc_sw128(sQ + (kk >> 2) * C::kQChunk + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = umma_desc_sw128(kbase + (kk >> 2) * C::kKChunk + (kk & 3) * 32, 16, 1024);
           umma_ss(tmem + sb * BN, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar(C::kBarS + sb));
-        return true;
-      };
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % ST;
-        if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) return false;
-        CA_EV(2, j);
-        const uint32_t kbase = sK + s * C::kKVBytes;
-        for (int g = 0; g < NQ; ++g)
-          if (!mma_s(j, g, kbase)) return false;
         CA_EV(10, j);
         umma_commit(bar(C::kBarKE + s));
         return true;
       };
-      // P V of tile j into accumulator g (P buffer g).
-      auto mma_pv = [&](int i, int g, int use, uint32_t vbase) -> bool {
+      // O[g] += P[i] V_i, P read from TMEM (S buffer i & 1, 16 columns per
+      // 16 keys: hi terms in the first 8, lo terms in the last 8).
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % ST;
+        const int g = og(i), use = ouse(i);
+        if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead)) return false;
         if (!mbar_wait(bar(C::kBarP + g), use & 1, dead)) return false;
+        // kSplit: P V[i - 1] done (frees the buffer S[i + 2] takes). Checked
+        // before P V[i] is issued, so the O barrier is at most one phase on.
+        if (SPLIT && i > 0 && !mbar_wait(bar(C::kBarO), (i - 1) & 1, dead)) return false;
         CA_EV(3, i);
         tc_fence_after();
-        const uint32_t pbase = sP + g * C::kPGroupBytes;
+        const uint32_t vbase = sV + s * C::kKVBytes;
+        const uint32_t pcol = tmem + (i % C::SB) * BN;
         const uint32_t dst = tmem + C::kOCol + g * HDP;
 #pragma unroll
         for (int term = 0; term < C::kPTerms; ++term) {
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t a = umma_desc_sw128(
-                pbase + term * C::kPTermBytes + (kk >> 2) * C::kPChunk + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = umma_desc_sw128(vbase + kk * 2048, C::kKChunk, 1024);
-            umma_ss(dst, a, bd, C::kIdescO, (use > 0 || kk > 0 || term > 0) ? 1u : 0u);
+            umma_ts(dst, pcol + kk * 16 + term * 8, bd, C::kIdescO,
+                    (use > 0 || kk > 0 || term > 0) ? 1u : 0u);
           }
         }
         umma_commit(bar(C::kBarO + g));
-        return true;
-      };
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % ST;
-        if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead)) return false;
-        CA_EV(4, i);
-        const uint32_t vbase = sV + s * C::kKVBytes;
-        if (PAIRQ) {
-          for (int g = 0; g < 2; ++g)
-            if (!mma_pv(i, g, i, vbase)) return false;
-        } else if (ALT) {
-          if (!mma_pv(i, i & 1, i >> 1, vbase)) return false;
-        } else {
-          if (!mma_pv(i, 0, i, vbase)) return false;
-        }
         CA_EV(11, i);
         umma_commit(bar(C::kBarVE + s));
         return true;
       };
-      // Order: S[0], S[1], then per tile j: P V[j] once P[j] is written and
-      // S[j+2] once the softmax has read S[j] out of its buffer (with PAIRQ
-      // each Q tile has two S buffers, so S[j+1] is already computing while
-      // the group works on S[j]).
+      // Order. Two S buffers (kAlt): S[0], S[1], then per tile j: P V[j]
+      // once P[j] is written, then S[j+2], which reuses P[j]'s buffer and
+      // waits for P V[j]; the other group's softmax covers the gap. More
+      // buffers: S[0..SB-2], then per tile j: P V[j], S[j+SB-1] (the buffer
+      // of P[j-1], whose P V is done or nearly so), so the tensor core runs
+      // P V[j] and the next S back to back, ahead of the softmax.
       if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead)) {
-        if constexpr (PAIRQ) {
-          bool ok = issue_s(0) && (n < 2 || issue_s(1));
-          for (int j = 0; ok && j < n; ++j) ok = issue_pv(j) && (j + 2 >= n || issue_s(j + 2));
-        } else {
-          bool ok = issue_s(0) && (n < 2 || issue_s(1));
-          for (int j = 0; ok && j < n; ++j) ok = (j + 2 >= n || issue_s(j + 2)) && issue_pv(j);
-        }
+        constexpr int kAhead = C::SB == 2 ? 2 : C::SB - 1;
+        bool ok = true;
+        for (int j = 0; ok && j < kAhead && j < n; ++j) ok = issue_s(j);
+        for (int j = 0; ok && j < n; ++j)
+          ok = issue_pv(j) && (j + kAhead >= n || issue_s(j + kAhead));
       }
       // Every MMA this thread issued completes before the role ends.
       umma_commit(bar(C::kBarF));
@@ -505,10 +492,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const int s_col0 = SPLIT ? grp * SC : 0;
     const uint32_t o_own = C::kOCol + grp * OC;
-    const int pg = SPLIT ? 0 : grp;
-    const uint32_t pbuf = sP + pg * C::kPGroupBytes;
+    const int pg = SPLIT ? 0 : grp;  // P barrier and O accumulator of this group
     const uint32_t xbar = bar(C::kBarX + wq);
-    const int t_local = t0 + (PAIRQ ? grp : 0) * p.QT + r / p.G;
+    const int t_local = t0 + r / p.G;
     const bool row_valid = r < p.R && t_local < q_len;
     const int gq = q_beg + (row_valid ? t_local : 0);
     int qpos = 0, qseq = 0, qpre = -1;
@@ -530,23 +516,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int kt = entry & 0x3fff;
       const int kind = entry >> 14;  // 0 full, 1 ragged end, 2 masked
       const bool partial = kind == 2;
-      const int sb = PAIRQ ? grp * 2 + (j & 1) : (j & 1);
-      mbar_wait(bar(C::kBarS + sb), (j >> 1) & 1, dead);
+      const int sb = j % C::SB;
+      mbar_wait(bar(C::kBarS + sb), (j / C::SB) & 1, dead);
       dead = __any_sync(0xffffffffu, dead);
       if (dead) break;
-      if (warp == 4 && lane == 0) CA_EV(5, j);
+      if ((warp & 3) == 2 && lane == 0) CA_EV(5, j);
       tc_fence_after();
       // S is read from TMEM twice, 32 columns at a time: pass 1 forms the row
-      // max, pass 2 exponentiates and stores P. No thread holds a whole row,
-      // which keeps the softmax warps well inside 168 registers.
+      // max, pass 2 exponentiates and writes P back over the columns it just
+      // read. No thread holds a whole row, which keeps the softmax warps well
+      // inside their registers.
       constexpr int LB = 32;
       const uint32_t s_addr = tmem + lane_off + sb * BN + s_col0;
       // Four forms of the same arithmetic, picked per tile (uniform):
       //   kFast     every key visible, plain scale: unrolled, FFMA + ex2
       //   kRagged   as kFast but keys at or past `nvalid` are masked
       //   kCapped   soft-cap (or negative scale) and no masks: unrolled
-      //   kGeneric  per-element visibility: compact rolled loop over 8-column
-      //             TMEM loads (cold: runs on a few tiles per CTA)
+      //   kGeneric  per-element visibility: compact rolled loops over 8- and
+      //             16-column TMEM loads (cold: runs on a few tiles per CTA)
       enum { kFast, kRagged, kCapped, kGeneric };
       const int form = (partial || (kind == 1 && !fast_ok)) ? kGeneric
                        : !fast_ok                        ? kCapped
@@ -587,14 +574,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             uint32_t sr[LB];
             tmem_ld32(s_addr + cb * LB, sr);
             tmem_wait_ld();
+            float v[LB];
 #pragma unroll
             for (int i = 0; i < LB; ++i) {
-              float v;
-              if constexpr (F == kFast) v = u2f(sr[i]);
-              else if constexpr (F == kRagged) v = cb * LB + i < nvalid ? u2f(sr[i]) : -INFINITY;
-              else v = sgn * u2f(sr[i]);  // kCapped: logit is monotonic in the raw score
-              mx8[i & 7] = fmaxf(mx8[i & 7], v);
+              if constexpr (F == kFast) v[i] = u2f(sr[i]);
+              else if constexpr (F == kRagged) v[i] = cb * LB + i < nvalid ? u2f(sr[i]) : -INFINITY;
+              else v[i] = sgn * u2f(sr[i]);  // kCapped: logit is monotonic in the raw score
             }
+#pragma unroll
+            for (int i = 0; i < LB; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], v[i]);
           }
         };
         if (form == kGeneric) {
@@ -616,7 +604,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         rmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       }
-      if (warp == 4 && lane == 0) CA_EV(6, j);
+      if ((warp & 3) == 2 && lane == 0) CA_EV(6, j);
       if constexpr (SPLIT) {
         // Combine with the partner warp (same rows, other key columns).
         float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
@@ -643,43 +631,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
 
-      // This group's P buffer and O are free once its previous P V completed.
-      if (used > 0) {
-        mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
-        dead = __any_sync(0xffffffffu, dead);
-        if (dead) break;
-        tc_fence_after();
-      }
-      if (warp == 4 && lane == 0) CA_EV(7, j);
-      // Pass 2: exponentiate 8 keys at a time and store them straight into P
-      // (row r: 128-byte rows of 64 keys, 16-byte units XOR-swizzled by r & 7).
+      if ((warp & 3) == 2 && lane == 0) CA_EV(7, j);
+      // Pass 2: exponentiate and write P into the S buffer, in the layout the
+      // P V MMA reads as its TMEM A operand: the 16 keys of block kk take
+      // columns 16 kk .. 16 kk + 15, bf16 pairs of the hi terms in the first 8
+      // and (PRECISE) of the lo terms in the last 8. Every block lands inside
+      // the columns it was read from, so no unread S is overwritten.
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-      auto store_p = [&](int key0, const uint32_t (&pk)[4], const uint32_t (&pl)[4]) {
-        const uint32_t addr =
-            pbuf + (key0 >> 6) * C::kPChunk + r * 128 + ((((key0 & 63) >> 3) ^ (r & 7)) << 4);
-        st_shared_v4(addr, pk[0], pk[1], pk[2], pk[3]);
-        if constexpr (C::PRECISE) st_shared_v4(addr + C::kPTermBytes, pl[0], pl[1], pl[2], pl[3]);
-      };
-      auto emit = [&](float p0, float p1, int q2, uint32_t (&pk)[4], uint32_t (&pl)[4]) {
-        sum4[q2] += p0 + p1;
-        pk[q2] = pack_bf16(p0, p1);
+      auto emit = [&](float p0, float p1, int q2, uint32_t& hi, uint32_t& lo) {
+        sum4[q2 & 3] += p0 + p1;
+        hi = pack_bf16(p0, p1);
         if constexpr (C::PRECISE) {
-          const float h0 = __uint_as_float(pk[q2] << 16);
-          const float h1 = __uint_as_float(pk[q2] & 0xffff0000u);
-          pl[q2] = pack_bf16(p0 - h0, p1 - h1);
+          const float h0 = __uint_as_float(hi << 16);
+          const float h1 = __uint_as_float(hi & 0xffff0000u);
+          lo = pack_bf16(p0 - h0, p1 - h1);
         }
       };
       if (form == kGeneric) {
 #pragma unroll 1
-        for (int c8 = 0; c8 < SC / 8; ++c8) {
-          uint32_t sr[8], pk[4], pl[4];
-          tmem_ld8(s_addr + c8 * 8, sr);
+        for (int c16 = 0; c16 < SC / 16; ++c16) {
+          uint32_t sr[16], hi[8], lo[8];
+          tmem_ld16(s_addr + c16 * 16, sr);
           tmem_wait_ld();
 #pragma unroll
-          for (int q2 = 0; q2 < 4; ++q2)
-            emit(ex2_approx(logit(sr[2 * q2], c8 * 8 + 2 * q2) - mu),
-                 ex2_approx(logit(sr[2 * q2 + 1], c8 * 8 + 2 * q2 + 1) - mu), q2, pk, pl);
-          store_p(s_col0 + c8 * 8, pk, pl);
+          for (int q2 = 0; q2 < 8; ++q2)
+            emit(ex2_approx(logit(sr[2 * q2], c16 * 16 + 2 * q2) - mu),
+                 ex2_approx(logit(sr[2 * q2 + 1], c16 * 16 + 2 * q2 + 1) - mu), q2, hi[q2],
+                 lo[q2]);
+          tmem_st8(s_addr + c16 * 16, hi);
+          if constexpr (C::PRECISE) tmem_st8(s_addr + c16 * 16 + 8, lo);
         }
       } else {
         auto pass2 = [&](auto form_c) {
@@ -690,11 +670,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tmem_ld32(s_addr + cb * LB, sr);
             tmem_wait_ld();
 #pragma unroll
-            for (int u = 0; u < LB / 8; ++u) {
-              uint32_t pk[4], pl[4];
+            for (int blk = 0; blk < LB / 16; ++blk) {
+              uint32_t hi[8], lo[8];
 #pragma unroll
-              for (int q2 = 0; q2 < 4; ++q2) {
-                const int i = u * 8 + q2 * 2;
+              for (int q2 = 0; q2 < 8; ++q2) {
+                const int i = blk * 16 + q2 * 2;
                 float x0, x1;
                 if constexpr (F == kCapped) {
                   x0 = logit_nm(sr[i]) - mu;
@@ -707,15 +687,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     x1 = cb * LB + i + 1 < nvalid ? x1 : -INFINITY;
                   }
                 }
-                // Pairs selected by kPolyPairs go through the FMA-pipe exp2
-                // (ex2_poly, never given -inf); measured break-even is low,
-                // so it is off.
-                if (F == kFast && ((kPolyPairs >> q2) & 1))
-                  emit(ex2_poly(x0), ex2_poly(x1), q2, pk, pl);
-                else
-                  emit(ex2_approx(x0), ex2_approx(x1), q2, pk, pl);
+                emit(ex2_approx(x0), ex2_approx(x1), q2, hi[q2], lo[q2]);
               }
-              store_p(s_col0 + cb * LB + u * 8, pk, pl);
+              tmem_st8(s_addr + cb * LB + blk * 16, hi);
+              if constexpr (C::PRECISE) tmem_st8(s_addr + cb * LB + blk * 16 + 8, lo);
             }
           }
         };
@@ -723,14 +698,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         else if (form == kRagged) pass2(std::integral_constant<int, kRagged>{});
         else pass2(std::integral_constant<int, kCapped>{});
       }
-      // S[j] is fully read: its buffer may take S[j + 2].
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C::kBarSF + sb));
       l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-      if (warp == 4 && lane == 0) CA_EV(8, j);
-      // Lazy correction of O (rare after the first tiles), once S is dead.
+      if ((warp & 3) == 2 && lane == 0) CA_EV(8, j);
+      // kAlt, two S buffers: this group's previous P V completed before S[j]
+      // was computed. kSplit: the previous P V (tile j - 1) may still run;
+      // wait for it. The wait also keeps the O barrier from running two
+      // phases ahead of any waiter (P V[j] cannot start before this warp's P
+      // arrival below). kAlt, four buffers: wait only before a correction.
+      if constexpr (SPLIT) {
+        if (used > 0) {
+          mbar_wait(bar(C::kBarO), (j - 1) & 1, dead);
+          dead = __any_sync(0xffffffffu, dead);
+          if (dead) break;
+          tc_fence_after();
+        }
+      }
+      // Lazy correction of O (rare after the first tiles).
       if (used > 0 && __any_sync(0xffffffffu, resc)) {
+        if constexpr (ALT && C::SB > 2) {
+          mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
+          dead = __any_sync(0xffffffffu, dead);
+          if (dead) break;
+          tc_fence_after();
+        }
 #pragma unroll 1
         for (int c = 0; c < OC / 32; ++c) {
           uint32_t o[32];
@@ -741,21 +731,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * corr);
           tmem_st32(ta, o);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      // P (and any corrected O) must be in TMEM before the P V MMA is issued.
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (warp == 4 && lane == 0) CA_EV(9, j);
+      if ((warp & 3) == 2 && lane == 0) CA_EV(9, j);
       if (lane == 0) mbar_arrive(bar(C::kBarP + pg));
       ++used;
     }
 
     // ------------------------------------------------------------ epilogue
-    // Wait for this group's last P V. kPairQ: the rows are the group's own.
-    // kAlt: merge the two groups' (max, sum, O) partials. kSplit: add the two
+    // Wait for this group's last P V. kAlt: merge the two groups' (max, sum, O) partials. kSplit: add the two
     // halves' row sums (same running max).
-    if (used > 0 && !dead) {
+    // kAlt: the merge exchange below borrows the K ring, so wait until every
+    // MMA is done (also covers a group that had no tile of its own).
+    if (ALT && n > 0 && !dead) {
+      mbar_wait(bar(C::kBarF), 0, dead);
+      dead = __any_sync(0xffffffffu, dead);
+      tc_fence_after();
+    } else if (used > 0 && !dead) {
       mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
       dead = __any_sync(0xffffffffu, dead);
       tc_fence_after();
@@ -764,13 +759,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     float s_me = 1.f, s_ot = 0.f, inv = __int_as_float(0x7fc00000);
     const int n_me = ALT ? (grp == 0 ? (n + 1) / 2 : n / 2) : n;
     const int n_ot = ALT ? (grp == 0 ? n / 2 : (n + 1) / 2) : 0;
-    if (have && PAIRQ) {
-      inv = 1.f / l;
-    } else if (have) {
-      float* xo = ALT ? reinterpret_cast<float*>(smem + C::kOffP + grp * C::kPGroupBytes)
-                      : reinterpret_cast<float*>(smem + C::kOffXch) + ((n & 1) * 2 + grp) * 128;
-      float* xp = ALT ? reinterpret_cast<float*>(smem + C::kOffP + (grp ^ 1) * C::kPGroupBytes)
-                      : reinterpret_cast<float*>(smem + C::kOffXch) + ((n & 1) * 2 + (grp ^ 1)) * 128;
+    if (have) {
+      // kAlt: [group][l, m][128] in the K ring, idle once every MMA is done.
+      float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
+      float* xo = ALT ? xch + grp * 256 : xch + ((n & 1) * 2 + grp) * 128;
+      float* xp = ALT ? xch + (grp ^ 1) * 256 : xch + ((n & 1) * 2 + (grp ^ 1)) * 128;
       xo[r] = l;
       if (ALT) xo[128 + r] = m;
       __syncwarp();
@@ -792,10 +785,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
     const int head = kvh * p.G + (r % p.G);
-    // Columns this warp writes: kPairQ all of its O; kAlt half of the columns
-    // from both accumulators; kSplit its own half.
-    constexpr int WC = PAIRQ ? HDP : HDP / 2;
-    const int col0 = PAIRQ ? 0 : grp * WC;
+    // Columns this warp writes: kAlt half of the columns from both
+    // accumulators; kSplit its own half.
+    constexpr int WC = HDP / 2;
+    const int col0 = grp * WC;
     const uint32_t o_me = ALT ? C::kOCol + grp * HDP + col0 : o_own;
     const uint32_t o_ot = C::kOCol + (grp ^ 1) * HDP + col0;
 #pragma unroll 1

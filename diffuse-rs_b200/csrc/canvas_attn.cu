@@ -89,7 +89,7 @@ struct Launch {
         return CA_ERR_CUDA;
       attr_done[dev] = true;
     }
-    const int n_qtiles = (max_sq + C::NQ * p->QT - 1) / (C::NQ * p->QT);
+    const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
     dim3 grid(n_qtiles, p->n_head_kv, p->batch);
     attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, *p);
     return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
@@ -172,24 +172,27 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
                    : 0;
 
   Launch L{a, &p, total_q, total_k, max_sq, max_sk, qrs, krs, st};
-  // One Q tile per CTA with alternating key tiles (head_dim <= 192) or split
-  // key columns (head_dim 256). The two-Q-tile mode (kPairQ, 64-key tiles)
-  // is correct but measured slower on B200 (733 vs 829 TFLOP/s at B8 S4096
-  // H16 hd128), so it is not dispatched.
-  constexpr bool pairq = false;
+  // One Q tile per CTA. head_dim <= 192: the two softmax groups alternate
+  // key tiles (kAlt). head_dim 256: they split every tile's key columns
+  // around one O, with three S buffers (kSplit). P lives in TMEM, so shared
+  // memory holds only Q and the K/V rings; ring depths fill what is left of
+  // 227 KB. (kSplit with three S buffers at head_dim 128 measured 746 vs
+  // 823 TFLOP/s for kAlt at B8 S4096 H16.)
   if (a->precise) {
-    if (hdp == 64) return pairq ? L.run<FwdCfg<64, 64, 3, true, kPairQ>>()
-                                : L.run<FwdCfg<64, 128, 2, true, kAlt>>();
-    if (hdp == 128) return pairq ? L.run<FwdCfg<128, 64, 2, true, kPairQ>>()
-                                 : L.run<FwdCfg<128, 64, 3, true, kAlt>>();
-    if (hdp == 192) return L.run<FwdCfg<192, 64, 2, true, kAlt>>();
+    if (hdp == 64) return L.run<FwdCfg<64, 128, 4, true, kAlt>>();
+    if (hdp == 128) return L.run<FwdCfg<128, 128, 3, true, kAlt>>();
+    if (hdp == 192) return L.run<FwdCfg<192, 64, 3, true, kAlt>>();
     return L.run<FwdCfg<256, 64, 2, true, kSplit>>();
   }
-  if (hdp == 64) return pairq ? L.run<FwdCfg<64, 64, 4, false, kPairQ>>()
-                              : L.run<FwdCfg<64, 128, 3, false, kAlt>>();
-  if (hdp == 128) return pairq ? L.run<FwdCfg<128, 64, 3, false, kPairQ>>()
-                               : L.run<FwdCfg<128, 128, 2, false, kAlt>>();
-  if (hdp == 192) return L.run<FwdCfg<192, 64, 2, false, kAlt>>();
+  if (hdp == 64) return L.run<FwdCfg<64, 128, 4, false, kAlt>>();
+#if CA_VARIANT == 1
+  if (hdp == 128) return L.run<FwdCfg<128, 64, 4, false, kAlt, 4>>();
+#elif CA_VARIANT == 2
+  if (hdp == 128) return L.run<FwdCfg<128, 64, 6, false, kAlt, 4>>();
+#else
+  if (hdp == 128) return L.run<FwdCfg<128, 128, 3, false, kAlt>>();
+#endif
+  if (hdp == 192) return L.run<FwdCfg<192, 64, 3, false, kAlt>>();
   return L.run<FwdCfg<256, 64, 2, false, kSplit>>();
 }
 
