@@ -7,13 +7,14 @@
 // (src/model/attention.rs:35-57, :106-186): per query row, softmax over every
 // visible key of scale * q.k, times V; rows with no visible key give NaN.
 //
-// Warp roles (320 threads, one CTA per SM):
-//   warp 0      lane 0: TMA producer of Q and the K ring; lane 1: the V ring
+// Warp roles (352 threads, one CTA per SM):
+//   warp 0      TMA producer of Q and the K ring (lane 0)
 //   warp 1      TMEM allocator + tcgen05.mma issuer (lane 0)
+//   warp 2      TMA producer of the V ring (lane 0)
 //   warps 0-1   prologue: build the list of key tiles that have any visible
 //               (query, key) pair, flagging tiles that need per-element masks
-//   warps 2-9   softmax, O correction and epilogue in two groups of four
-//               warps (2-5 and 6-9); warp w reaches TMEM lanes 32 (w % 4)..+31
+//   warps 3-10  softmax, O correction and epilogue in two groups of four
+//               warps (3-6 and 7-10); warp w reaches TMEM lanes 32 (w % 4)..+31
 //
 // Pipeline per visible key tile j (S double-buffered in TMEM; P in TMEM too):
 //   S[j&1] = Q K_j^T           (tcgen05.mma, SS, fp32 accumulate in TMEM)
@@ -50,12 +51,23 @@ __device__ long long g_trace[16][64];
     if (blockIdx.x == CA_TRACE_X && blockIdx.y == 3 && blockIdx.z == 1 && (j) < 64)          \
       g_trace[kind][j] = clock64();                                                 \
   } while (0)
+// Per softmax warp (8 warps x 4 events x 64 tiles).
+__device__ long long g_trace_w[8][4][64];
+#define CA_EVW(e, j)                                                                    \
+  do {                                                                                  \
+    if (lane == 0 && blockIdx.x == CA_TRACE_X && blockIdx.y == 3 && blockIdx.z == 1 &&  \
+        (j) < 64)                                                                       \
+      g_trace_w[warp - 3][e][j] = clock64();                                            \
+  } while (0)
 #else
+#define CA_EVW(e, j) \
+  do {               \
+  } while (0)
 #define CA_EV(kind, j) \
   do {                 \
   } while (0)
 #endif
-constexpr int kFwdThreads = 320;  // 2 control warps + 8 softmax warps
+constexpr int kFwdThreads = 352;  // 3 control warps + 8 softmax warps
 
 struct FwdParams {
   void* out;
@@ -88,7 +100,7 @@ struct FwdParams {
 enum FwdMode { kSplit = 0, kAlt = 1 };
 
 
-template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_, int SB_ = (MODE_ == 0 ? 3 : 2)>
+template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_>
 struct FwdCfg {
   static constexpr int HDP = HDP_;  // head_dim padded to a multiple of 64
   static constexpr int BN = BN_;    // keys per tile
@@ -102,9 +114,7 @@ struct FwdCfg {
   static constexpr int kPTerms = PRECISE ? 2 : 1;
   // S buffers in TMEM (P overwrites S in place). kSplit keeps one O, which
   // leaves room for a third buffer: S runs two tiles ahead of the softmax.
-  // kAlt with 64-key tiles fits four: each group double-buffers its S.
-  static constexpr int SB = SB_;
-  static_assert(SPLIT ? SB == 3 : (SB == 2 || SB == 4), "S buffering");
+  static constexpr int SB = SPLIT ? 3 : 2;
   static constexpr int kChunks = HDP / 64;  // 128-byte swizzle atoms along head_dim
   static constexpr int kQChunk = 128 * 128;
   static constexpr int kKChunk = BN * 128;
@@ -363,12 +373,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int n = misc[1];
   bool dead = false;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 2) {
     // ------------------------------------------------------------ producers
-    // Lane 0 streams Q and the K tiles, lane 1 the V tiles: the two rings
-    // drain at different times (K after Q K^T, V after P V).
-    if (lane < 2) {
-      const bool is_k = lane == 0;
+    // Warp 0 streams Q and the K tiles, warp 2 the V tiles. The two rings
+    // drain at different times (K after Q K^T, V after P V); as two lanes of
+    // one warp their diverged waits delayed each other's loads.
+    if (lane == 0) {
+      const bool is_k = warp == 0;
       const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
       const uint32_t ring = is_k ? sK : sV;
       const int full = is_k ? C::kBarK : C::kBarV;
@@ -410,15 +421,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int s = j % ST;
         const int sb = j % C::SB;
         if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) return false;
-#ifndef CA_INORDER
-        if (ALT && j >= C::SB &&
-            !mbar_wait(bar(C::kBarO + og(j - C::SB)), ouse(j - C::SB) & 1, dead))
+        CA_EV(13, j);
+        if (ALT && j >= 2 && !mbar_wait(bar(C::kBarO + og(j - 2)), ouse(j - 2) & 1, dead))
           return false;
-#else
-        if (ALT && C::SB > 2 && j >= C::SB &&
-            !mbar_wait(bar(C::kBarO + og(j - C::SB)), ouse(j - C::SB) & 1, dead))
-          return false;
-#endif
         CA_EV(2, j);
         tc_fence_after();
         const uint32_t kbase = sK + s * C::kKVBytes;
@@ -439,6 +444,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int s = i % ST;
         const int g = og(i), use = ouse(i);
         if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead)) return false;
+        CA_EV(12, i);
         if (!mbar_wait(bar(C::kBarP + g), use & 1, dead)) return false;
         // kSplit: P V[i - 1] done (frees the buffer S[i + 2] takes). Checked
         // before P V[i] is issued, so the O barrier is at most one phase on.
@@ -462,18 +468,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         umma_commit(bar(C::kBarVE + s));
         return true;
       };
-      // Order. Two S buffers (kAlt): S[0], S[1], then per tile j: P V[j]
-      // once P[j] is written, then S[j+2], which reuses P[j]'s buffer and
-      // waits for P V[j]; the other group's softmax covers the gap. More
-      // buffers: S[0..SB-2], then per tile j: P V[j], S[j+SB-1] (the buffer
-      // of P[j-1], whose P V is done or nearly so), so the tensor core runs
-      // P V[j] and the next S back to back, ahead of the softmax.
+      // Order: S[0], S[1], then per tile j: P V[j] once P[j] is written,
+      // then S[j+2]. kAlt: S[j+2] reuses P[j]'s buffer and waits for P V[j];
+      // the other group's softmax covers the gap. kSplit: S[j+2] takes the
+      // buffer of P[j-1], so the tensor core runs P V[j] and S[j+2] back to
+      // back while the softmax works on S[j+1].
       if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead)) {
-        constexpr int kAhead = C::SB == 2 ? 2 : C::SB - 1;
-        bool ok = true;
-        for (int j = 0; ok && j < kAhead && j < n; ++j) ok = issue_s(j);
-        for (int j = 0; ok && j < n; ++j)
-          ok = issue_pv(j) && (j + kAhead >= n || issue_s(j + kAhead));
+        bool ok = issue_s(0) && (n < 2 || issue_s(1));
+        for (int j = 0; ok && j < n; ++j) ok = issue_pv(j) && (j + 2 >= n || issue_s(j + 2));
       }
       // Every MMA this thread issued completes before the role ends.
       umma_commit(bar(C::kBarF));
@@ -482,12 +484,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    // Warps 2..9: warp w reaches TMEM lanes 32 (w % 4) .. +31, so each lane
-    // quarter q has two warps, one per group (grp 0: warps 2-5, 1: 6-9).
+    // Warps 3..10: warp w reaches TMEM lanes 32 (w % 4) .. +31, so each lane
+    // quarter q has two warps, one per group (grp 0: warps 3-6, 1: 7-10).
     constexpr int SC = SPLIT ? BN / 2 : BN;    // S columns per thread per tile
     constexpr int OC = SPLIT ? HDP / 2 : HDP;  // O columns this group owns
     const int wq = warp & 3;
-    const int grp = (warp - 2) >> 2;
+    const int grp = (warp - 3) >> 2;
     const int r = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const int s_col0 = SPLIT ? grp * SC : 0;
@@ -521,11 +523,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       dead = __any_sync(0xffffffffu, dead);
       if (dead) break;
       if ((warp & 3) == 2 && lane == 0) CA_EV(5, j);
+      CA_EVW(0, j);
       tc_fence_after();
-      // S is read from TMEM twice, 32 columns at a time: pass 1 forms the row
-      // max, pass 2 exponentiates and writes P back over the columns it just
-      // read. No thread holds a whole row, which keeps the softmax warps well
-      // inside their registers.
+      // Each thread reads its row of S from TMEM once (32-column loads, one
+      // wait) and keeps it in registers: pass 1 forms the row max, pass 2
+      // exponentiates and writes P back over the columns of S. The masked
+      // form instead streams 8- and 16-column pieces twice (cold path).
       constexpr int LB = 32;
       const uint32_t s_addr = tmem + lane_off + sb * BN + s_col0;
       // Four forms of the same arithmetic, picked per tile (uniform):
@@ -562,6 +565,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
       // Pass 1: row max over this thread's columns (8 independent chains).
       // Each form is its own loop (the form is a template constant there).
+      uint32_t srow[SC];
       float rmax;
       {
         float mx8[8];
@@ -569,11 +573,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
         auto pass1 = [&](auto form_c) {
           constexpr int F = decltype(form_c)::value;
-#pragma unroll 1
+#pragma unroll
+          for (int cb = 0; cb < SC / LB; ++cb)
+            tmem_ld32(s_addr + cb * LB, *reinterpret_cast<uint32_t(*)[LB]>(&srow[cb * LB]));
+          tmem_wait_ld();
+#pragma unroll
           for (int cb = 0; cb < SC / LB; ++cb) {
-            uint32_t sr[LB];
-            tmem_ld32(s_addr + cb * LB, sr);
-            tmem_wait_ld();
+            const uint32_t* sr = &srow[cb * LB];
             float v[LB];
 #pragma unroll
             for (int i = 0; i < LB; ++i) {
@@ -605,6 +611,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       }
       if ((warp & 3) == 2 && lane == 0) CA_EV(6, j);
+      CA_EVW(1, j);
       if constexpr (SPLIT) {
         // Combine with the partner warp (same rows, other key columns).
         float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
@@ -664,11 +671,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       } else {
         auto pass2 = [&](auto form_c) {
           constexpr int F = decltype(form_c)::value;
-#pragma unroll 1
+#pragma unroll
           for (int cb = 0; cb < SC / LB; ++cb) {
-            uint32_t sr[LB];
-            tmem_ld32(s_addr + cb * LB, sr);
-            tmem_wait_ld();
+            const uint32_t* sr = &srow[cb * LB];
 #pragma unroll
             for (int blk = 0; blk < LB / 16; ++blk) {
               uint32_t hi[8], lo[8];
@@ -700,11 +705,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
       if ((warp & 3) == 2 && lane == 0) CA_EV(8, j);
-      // kAlt, two S buffers: this group's previous P V completed before S[j]
-      // was computed. kSplit: the previous P V (tile j - 1) may still run;
-      // wait for it. The wait also keeps the O barrier from running two
-      // phases ahead of any waiter (P V[j] cannot start before this warp's P
-      // arrival below). kAlt, four buffers: wait only before a correction.
+      CA_EVW(2, j);
+      // kAlt: this group's previous P V completed before S[j] was computed.
+      // kSplit: the previous P V (tile j - 1) may still run; wait for it. The
+      // wait also keeps the O barrier from running two phases ahead of any
+      // waiter (P V[j] cannot start before this warp's P arrival below).
       if constexpr (SPLIT) {
         if (used > 0) {
           mbar_wait(bar(C::kBarO), (j - 1) & 1, dead);
@@ -715,12 +720,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       // Lazy correction of O (rare after the first tiles).
       if (used > 0 && __any_sync(0xffffffffu, resc)) {
-        if constexpr (ALT && C::SB > 2) {
-          mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
-          dead = __any_sync(0xffffffffu, dead);
-          if (dead) break;
-          tc_fence_after();
-        }
 #pragma unroll 1
         for (int c = 0; c < OC / 32; ++c) {
           uint32_t o[32];
@@ -737,6 +736,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if ((warp & 3) == 2 && lane == 0) CA_EV(9, j);
+      CA_EVW(3, j);
       if (lane == 0) mbar_arrive(bar(C::kBarP + pg));
       ++used;
     }

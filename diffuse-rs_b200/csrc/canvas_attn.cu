@@ -185,13 +185,7 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
     return L.run<FwdCfg<256, 64, 2, true, kSplit>>();
   }
   if (hdp == 64) return L.run<FwdCfg<64, 128, 4, false, kAlt>>();
-#if CA_VARIANT == 1
-  if (hdp == 128) return L.run<FwdCfg<128, 64, 4, false, kAlt, 4>>();
-#elif CA_VARIANT == 2
-  if (hdp == 128) return L.run<FwdCfg<128, 64, 6, false, kAlt, 4>>();
-#else
   if (hdp == 128) return L.run<FwdCfg<128, 128, 3, false, kAlt>>();
-#endif
   if (hdp == 192) return L.run<FwdCfg<192, 64, 3, false, kAlt>>();
   return L.run<FwdCfg<256, 64, 2, false, kSplit>>();
 }
@@ -548,6 +542,9 @@ const char* ca_version(void) { return "canvas_attn 0.1.0 sm_100a"; }
 // Diagnostic builds only: copies the recorded event timestamps to `dst`.
 int ca_debug_trace(long long* dst) {
   return cudaMemcpyFromSymbol(dst, ca::g_trace, sizeof(ca::g_trace)) == cudaSuccess ? 0 : -3;
+}
+int ca_debug_trace_w(long long* dst) {
+  return cudaMemcpyFromSymbol(dst, ca::g_trace_w, sizeof(ca::g_trace_w)) == cudaSuccess ? 0 : -3;
 }
 #endif
 
