@@ -181,6 +181,27 @@ __device__ __forceinline__ float tanh_via_exp2(float x) {
   return 1.f - __fdividef(2.f, e + 1.f);
 }
 
+// tanh(u) = u * P(u^2) for |u| <= kTanhPolyMax: P of degree 5 in u^2,
+// weighted least squares (relative error) on Chebyshev nodes in u^2, fitted
+// for this kernel; max abs error 5.3e-8 and max relative error 1.0e-7 in
+// float32 Horner evaluation. No MUFU op. Used for soft-cap tiles whose
+// scaled scores all lie in range (with QK-norm, nearly every tile).
+constexpr float kTanhPolyMax = 0.625f;
+constexpr float kTanhC1 = -0.3333325982093811f;
+constexpr float kTanhC2 = 0.13331091403961182f;
+constexpr float kTanhC3 = -0.053718484938144684f;
+constexpr float kTanhC4 = 0.020583488047122955f;
+constexpr float kTanhC5 = -0.005652355030179024f;
+__device__ __forceinline__ float tanh_poly(float u) {
+  const float w = u * u;
+  float p = fmaf(kTanhC5, w, kTanhC4);
+  p = fmaf(p, w, kTanhC3);
+  p = fmaf(p, w, kTanhC2);
+  p = fmaf(p, w, kTanhC1);
+  p = fmaf(p, w, 1.f);
+  return u * p;
+}
+
 }  // namespace ca
 
 namespace ca {
@@ -535,10 +556,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       //   kFast     every key visible, plain scale: unrolled, FFMA + ex2
       //   kRagged   as kFast but keys at or past `nvalid` are masked
       //   kCapped   soft-cap (or negative scale) and no masks: unrolled
+      //   kCapPoly  kCapped whose scaled scores all lie where tanh_poly is
+      //             exact (decided after pass 1): no MUFU op in the tanh
       //   kGeneric  per-element visibility: compact rolled loops over 8- and
       //             16-column TMEM loads (cold: runs on a few tiles per CTA)
-      enum { kFast, kRagged, kCapped, kGeneric };
-      const int form = (partial || (kind == 1 && !fast_ok)) ? kGeneric
+      enum { kFast, kRagged, kCapped, kGeneric, kCapPoly };
+      int form = (partial || (kind == 1 && !fast_ok)) ? kGeneric
                        : !fast_ok                        ? kCapped
                        : kind == 1                       ? kRagged
                                                          : kFast;
@@ -567,6 +590,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // Each form is its own loop (the form is a template constant there).
       uint32_t srow[SC];
       float rmax;
+      float amax = 0.f;  // kCapped: largest |raw score|
       {
         float mx8[8];
 #pragma unroll
@@ -589,6 +613,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
 #pragma unroll
             for (int i = 0; i < LB; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], v[i]);
+            if constexpr (F == kCapped) {
+#pragma unroll
+              for (int i = 0; i < LB; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            }
           }
         };
         if (form == kGeneric) {
@@ -630,6 +658,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       else if (form == kCapped) mcand = rmax == -INFINITY ? rmax : logit_nm(f2u(sgn * rmax));
       else mcand = rmax;
 
+      // Soft-cap tiles whose scaled scores all lie in tanh_poly's range (per
+      // warp; the two warps of a kSplit pair may choose differently, both
+      // forms give the same logits to ~1e-7).
+      if (form == kCapped && p.softcap != 0.f &&
+          __all_sync(0xffffffffu, amax * fabsf(scale_cap) <= kTanhPolyMax))
+        form = kCapPoly;
       const bool resc = mcand > m + 8.f;
       float corr = 1.f;
       if (resc) {
@@ -684,6 +718,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 if constexpr (F == kCapped) {
                   x0 = logit_nm(sr[i]) - mu;
                   x1 = logit_nm(sr[i + 1]) - mu;
+                } else if constexpr (F == kCapPoly) {
+                  x0 = fmaf(cap_l2, tanh_poly(u2f(sr[i]) * scale_cap), -mu);
+                  x1 = fmaf(cap_l2, tanh_poly(u2f(sr[i + 1]) * scale_cap), -mu);
                 } else {
                   x0 = fmaf(u2f(sr[i]), sl2, -mu);
                   x1 = fmaf(u2f(sr[i + 1]), sl2, -mu);
@@ -701,6 +738,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         };
         if (form == kFast) pass2(std::integral_constant<int, kFast>{});
         else if (form == kRagged) pass2(std::integral_constant<int, kRagged>{});
+        else if (form == kCapPoly) pass2(std::integral_constant<int, kCapPoly>{});
         else pass2(std::integral_constant<int, kCapped>{});
       }
       l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
