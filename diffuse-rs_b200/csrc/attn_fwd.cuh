@@ -528,6 +528,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     const float sl2 = p.scale_log2;
     const bool fast_ok = p.softcap == 0.f && sl2 >= 0.f;
+    // The sliding window is the only mask and positions are contiguous:
+    // visibility within a tile is a band test on the key index.
+    // (window 0 makes every key invisible: left to the generic form.)
+    const bool band_ok = p.window != kNoWindow && p.window > 0 && !p.k_pos && !p.k_seq &&
+                         !p.q_seq && !p.q_prefix && p.causal_prefix < 0;
     // Soft-cap: logit = cap * tanh(score * scale / cap), in log2 units.
     const float scale_cap = p.softcap != 0.f ? p.scale / p.softcap : 0.f;
     const float cap_l2 = p.softcap * 1.4426950408889634f;
@@ -538,7 +543,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int entry = list[j];
       const int kt = entry & 0x3fff;
       const int kind = entry >> 14;  // 0 full, 1 ragged end, 2 masked
-      const bool partial = kind == 2;
       const int sb = j % C::SB;
       mbar_wait(bar(C::kBarS + sb), (j / C::SB) & 1, dead);
       dead = __any_sync(0xffffffffu, dead);
@@ -552,20 +556,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // form instead streams 8- and 16-column pieces twice (cold path).
       constexpr int LB = 32;
       const uint32_t s_addr = tmem + lane_off + sb * BN + s_col0;
-      // Four forms of the same arithmetic, picked per tile (uniform):
-      //   kFast     every key visible, plain scale: unrolled, FFMA + ex2
-      //   kRagged   as kFast but keys at or past `nvalid` are masked
-      //   kCapped   soft-cap (or negative scale) and no masks: unrolled
-      //   kCapPoly  kCapped whose scaled scores all lie where tanh_poly is
-      //             exact (decided after pass 1): no MUFU op in the tanh
-      //   kGeneric  per-element visibility: compact rolled loops over 8- and
-      //             16-column TMEM loads (cold: runs on a few tiles per CTA)
-      enum { kFast, kRagged, kCapped, kGeneric, kCapPoly };
-      int form = (partial || (kind == 1 && !fast_ok)) ? kGeneric
-                       : !fast_ok                        ? kCapped
-                       : kind == 1                       ? kRagged
-                                                         : kFast;
-      const int nvalid = kind == 1 ? k_len - kt * BN - s_col0 : SC;
+      // The arithmetic is picked per tile (uniform) as a value transform and
+      // a mask, each loop unrolled with both as template constants:
+      //   value  kPlain    s * scale (scale >= 0, no soft-cap): FFMA + ex2
+      //          kCap      soft-cap (or negative scale): exact tanh
+      //          kCapPoly  kCap whose scaled scores all lie where tanh_poly
+      //                    is exact (decided after pass 1): no MUFU op
+      //   mask   kNone     every key of the tile visible
+      //          kRagged   keys at or past `nvalid` masked (sequence end)
+      //          kBand     |q pos - key| < window, positions contiguous (the
+      //                    sliding window is the only mask): integer test
+      // Other masks (seq ids, prefixes, explicit key positions) take the
+      // generic form: compact rolled loops over 8- and 16-column TMEM loads
+      // with per-element visible() (cold: a few tiles per CTA).
+      enum { kPlain, kCap, kCapPoly };
+      enum { kNone, kRagged, kBand, kGenericMask };
+      int val = fast_ok ? kPlain : kCap;
+      const int msk = kind == 0 ? kNone : kind == 1 ? kRagged : band_ok ? kBand : kGenericMask;
+      const bool generic = msk == kGenericMask;
+      const int nvalid = k_len - kt * BN - s_col0;  // keys of this thread's columns
+      // kBand: key i of the thread's columns is visible iff
+      // (unsigned)(band0 - i) <= band2, i.e. |qpos - key| < window.
+      const int band0 = qpos - (kt * BN + s_col0) + p.window - 1;
+      const uint32_t band2 = 2u * static_cast<uint32_t>(p.window) - 2u;
       const float sgn = p.scale < 0.f ? -1.f : 1.f;
       // Scaled log2-domain logit without masks (soft-cap, any scale sign).
       auto logit_nm = [&](uint32_t bits) -> float {
@@ -585,18 +598,46 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         return ok ? t : -INFINITY;
       };
+      // Visibility of column i under mask M (compile-time M, constant i).
+      auto vis = [&](auto msk_c, int i) -> bool {
+        constexpr int M = decltype(msk_c)::value;
+        if constexpr (M == kNone) return true;
+        else if constexpr (M == kRagged) return i < nvalid;
+        else return i < nvalid && static_cast<uint32_t>(band0 - i) <= band2;
+      };
+      // Calls f(value, mask) with the tile's forms as template constants.
+      auto dispatch = [&](auto f) {
+        using P0 = std::integral_constant<int, kPlain>;
+        using P1 = std::integral_constant<int, kCap>;
+        using P2 = std::integral_constant<int, kCapPoly>;
+        using M0 = std::integral_constant<int, kNone>;
+        using M1 = std::integral_constant<int, kRagged>;
+        using M2 = std::integral_constant<int, kBand>;
+        if (val == kPlain) {
+          if (msk == kNone) f(P0{}, M0{});
+          else if (msk == kRagged) f(P0{}, M1{});
+          else f(P0{}, M2{});
+        } else if (val == kCap) {
+          if (msk == kNone) f(P1{}, M0{});
+          else if (msk == kRagged) f(P1{}, M1{});
+          else f(P1{}, M2{});
+        } else {
+          if (msk == kNone) f(P2{}, M0{});
+          else if (msk == kRagged) f(P2{}, M1{});
+          else f(P2{}, M2{});
+        }
+      };
 
       // Pass 1: row max over this thread's columns (8 independent chains).
-      // Each form is its own loop (the form is a template constant there).
       uint32_t srow[SC];
       float rmax;
-      float amax = 0.f;  // kCapped: largest |raw score|
+      float amax = 0.f;  // kCap: largest |raw score| among visible keys
       {
         float mx8[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
-        auto pass1 = [&](auto form_c) {
-          constexpr int F = decltype(form_c)::value;
+        auto pass1 = [&](auto val_c, auto msk_c) {
+          constexpr int V = decltype(val_c)::value;
 #pragma unroll
           for (int cb = 0; cb < SC / LB; ++cb)
             tmem_ld32(s_addr + cb * LB, *reinterpret_cast<uint32_t(*)[LB]>(&srow[cb * LB]));
@@ -607,19 +648,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             float v[LB];
 #pragma unroll
             for (int i = 0; i < LB; ++i) {
-              if constexpr (F == kFast) v[i] = u2f(sr[i]);
-              else if constexpr (F == kRagged) v[i] = cb * LB + i < nvalid ? u2f(sr[i]) : -INFINITY;
-              else v[i] = sgn * u2f(sr[i]);  // kCapped: logit is monotonic in the raw score
+              // kCap: the logit is monotonic in sgn * raw score.
+              const float x = V == kPlain ? u2f(sr[i]) : sgn * u2f(sr[i]);
+              v[i] = vis(msk_c, cb * LB + i) ? x : -INFINITY;
             }
 #pragma unroll
             for (int i = 0; i < LB; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], v[i]);
-            if constexpr (F == kCapped) {
+            if constexpr (V == kCap) {
 #pragma unroll
-              for (int i = 0; i < LB; ++i) amax = fmaxf(amax, fabsf(v[i]));
+              for (int i = 0; i < LB; ++i)
+                amax = fmaxf(amax, vis(msk_c, cb * LB + i) ? fabsf(v[i]) : 0.f);
             }
           }
         };
-        if (form == kGeneric) {
+        if (generic) {
 #pragma unroll 1
           for (int c8 = 0; c8 < SC / 8; ++c8) {
             uint32_t sr[8];
@@ -628,12 +670,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(mx8[i], logit(sr[i], c8 * 8 + i));
           }
-        } else if (form == kFast) {
-          pass1(std::integral_constant<int, kFast>{});
-        } else if (form == kRagged) {
-          pass1(std::integral_constant<int, kRagged>{});
         } else {
-          pass1(std::integral_constant<int, kCapped>{});
+          dispatch(pass1);
         }
         rmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
@@ -651,19 +689,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (dead) break;
         rmax = fmaxf(rmax, xch[((j & 1) * 2 + (grp ^ 1)) * 128 + r]);
       }
-      // kFast / kRagged maxima are raw scores; kCapped's is sgn * raw score
-      // (the soft-capped logit is monotonic in it); kGeneric's is a logit.
+      // Plain maxima are raw scores; kCap's is sgn * raw score (the soft-
+      // capped logit is monotonic in it); the generic form's is a logit.
       float mcand;
-      if (form == kFast || form == kRagged) mcand = rmax * sl2;
-      else if (form == kCapped) mcand = rmax == -INFINITY ? rmax : logit_nm(f2u(sgn * rmax));
-      else mcand = rmax;
-
+      if (generic) mcand = rmax;
+      else if (val == kPlain) mcand = rmax * sl2;
+      else mcand = rmax == -INFINITY ? rmax : logit_nm(f2u(sgn * rmax));
       // Soft-cap tiles whose scaled scores all lie in tanh_poly's range (per
       // warp; the two warps of a kSplit pair may choose differently, both
       // forms give the same logits to ~1e-7).
-      if (form == kCapped && p.softcap != 0.f &&
+      if (!generic && val == kCap && p.softcap != 0.f &&
           __all_sync(0xffffffffu, amax * fabsf(scale_cap) <= kTanhPolyMax))
-        form = kCapPoly;
+        val = kCapPoly;
       const bool resc = mcand > m + 8.f;
       float corr = 1.f;
       if (resc) {
@@ -688,7 +725,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           lo = pack_bf16(p0 - h0, p1 - h1);
         }
       };
-      if (form == kGeneric) {
+      if (generic) {
 #pragma unroll 1
         for (int c16 = 0; c16 < SC / 16; ++c16) {
           uint32_t sr[16], hi[8], lo[8];
@@ -703,8 +740,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if constexpr (C::PRECISE) tmem_st8(s_addr + c16 * 16 + 8, lo);
         }
       } else {
-        auto pass2 = [&](auto form_c) {
-          constexpr int F = decltype(form_c)::value;
+        auto pass2 = [&](auto val_c, auto msk_c) {
+          constexpr int V = decltype(val_c)::value;
+          constexpr int M = decltype(msk_c)::value;
 #pragma unroll
           for (int cb = 0; cb < SC / LB; ++cb) {
             const uint32_t* sr = &srow[cb * LB];
@@ -715,19 +753,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               for (int q2 = 0; q2 < 8; ++q2) {
                 const int i = blk * 16 + q2 * 2;
                 float x0, x1;
-                if constexpr (F == kCapped) {
+                if constexpr (V == kCap) {
                   x0 = logit_nm(sr[i]) - mu;
                   x1 = logit_nm(sr[i + 1]) - mu;
-                } else if constexpr (F == kCapPoly) {
+                } else if constexpr (V == kCapPoly) {
                   x0 = fmaf(cap_l2, tanh_poly(u2f(sr[i]) * scale_cap), -mu);
                   x1 = fmaf(cap_l2, tanh_poly(u2f(sr[i + 1]) * scale_cap), -mu);
                 } else {
                   x0 = fmaf(u2f(sr[i]), sl2, -mu);
                   x1 = fmaf(u2f(sr[i + 1]), sl2, -mu);
-                  if constexpr (F == kRagged) {
-                    x0 = cb * LB + i < nvalid ? x0 : -INFINITY;
-                    x1 = cb * LB + i + 1 < nvalid ? x1 : -INFINITY;
-                  }
+                }
+                if constexpr (M != kNone) {
+                  x0 = vis(msk_c, cb * LB + i) ? x0 : -INFINITY;
+                  x1 = vis(msk_c, cb * LB + i + 1) ? x1 : -INFINITY;
                 }
                 emit(ex2_approx(x0), ex2_approx(x1), q2, hi[q2], lo[q2]);
               }
@@ -736,10 +774,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
           }
         };
-        if (form == kFast) pass2(std::integral_constant<int, kFast>{});
-        else if (form == kRagged) pass2(std::integral_constant<int, kRagged>{});
-        else if (form == kCapPoly) pass2(std::integral_constant<int, kCapPoly>{});
-        else pass2(std::integral_constant<int, kCapped>{});
+        dispatch(pass2);
       }
       l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
       if ((warp & 3) == 2 && lane == 0) CA_EV(8, j);
