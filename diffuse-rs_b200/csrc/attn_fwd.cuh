@@ -89,7 +89,8 @@ struct FwdParams {
   float scale;
   float scale_log2;   // scale * log2(e)
   float softcap;      // 0 = off
-  int any_mask;       // any of: positions, seq ids, prefixes, window, causal prefix
+  int any_mask;       // any of: seq ids, prefixes, window, causal prefix (positions
+                      // alone mask nothing: they matter only to those masks)
 };
 
 // Softmax organisation of a CTA (see the file comment):
@@ -237,6 +238,7 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
   const int lane = tid64 & 31;
   const int w = tid64 >> 5;  // 0..1
   const int n_kt = (k_len + C::BN - 1) / C::BN;
+  if (tid64 == 0) CA_EV(15, 4);
   if (!p.any_mask) {
     for (int kt = tid64; kt < n_kt; kt += 64)
       flags[kt] = ((kt + 1) * C::BN <= k_len) ? 1 : 3;
@@ -249,15 +251,29 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
     }
     named_bar_sync(1, 64);
     const int nt = min(span, q_len - t0);  // query tokens of this CTA
+    // Per-thread partials, one warp reduction each, one shared atomic per
+    // warp (the loads of all tokens are independent and overlap).
+    int pmin = INT_MAX, pmax = INT_MIN, smin = INT_MAX, smax = INT_MIN, cpmin = INT_MAX, ncaus = 0;
     for (int t = tid64; t < nt; t += 64) {
       const int tl = t0 + t;
       const int g = q_beg + tl;
       const int qp = p.q_pos ? p.q_pos[g] : tl;
       const int qsq = p.q_seq ? p.q_seq[g] : 0;
       const int pre = p.q_prefix ? p.q_prefix[g] : p.causal_prefix;
-      atomicMin(&qs[0], qp); atomicMax(&qs[1], qp);
-      atomicMin(&qs[2], qsq); atomicMax(&qs[3], qsq);
-      if (pre >= 0 && qp < pre) { atomicMin(&qs[4], qp); atomicAdd(&qs[5], 1); }
+      pmin = min(pmin, qp); pmax = max(pmax, qp);
+      smin = min(smin, qsq); smax = max(smax, qsq);
+      if (pre >= 0 && qp < pre) { cpmin = min(cpmin, qp); ++ncaus; }
+    }
+    pmin = __reduce_min_sync(0xffffffffu, pmin);
+    pmax = __reduce_max_sync(0xffffffffu, pmax);
+    smin = __reduce_min_sync(0xffffffffu, smin);
+    smax = __reduce_max_sync(0xffffffffu, smax);
+    cpmin = __reduce_min_sync(0xffffffffu, cpmin);
+    ncaus = __reduce_add_sync(0xffffffffu, ncaus);
+    if (lane == 0) {
+      atomicMin(&qs[0], pmin); atomicMax(&qs[1], pmax);
+      atomicMin(&qs[2], smin); atomicMax(&qs[3], smax);
+      atomicMin(&qs[4], cpmin); atomicAdd(&qs[5], ncaus);
     }
     named_bar_sync(1, 64);
     const long long qpmin = qs[0], qpmax = qs[1];
@@ -300,7 +316,9 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
       }
     }
   }
+  if (tid64 == 0) CA_EV(15, 5);
   named_bar_sync(1, 64);
+  if (tid64 == 0) CA_EV(15, 6);
   if (w == 0) {
     int count = 0;
     for (int base = 0; base < n_kt; base += 32) {
@@ -316,6 +334,7 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
       count += __popc(ball);
     }
     if (lane == 0) misc[1] = count;
+    if (lane == 0) CA_EV(15, 7);
   }
 }
 
@@ -349,6 +368,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   seq_range(p, b, q_beg, q_len, k_beg, k_len);
   const int t0 = qtile * p.QT;  // first query token of this CTA
   if (t0 >= q_len) return;           // uniform across the CTA
+  if (threadIdx.x == 0) CA_EV(14, 0);
 
   const uint32_t sQ = smem_u32(smem + C::kOffQ);
   const uint32_t sK = smem_u32(smem + C::kOffK);
@@ -375,21 +395,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int i = 0; i < 4; ++i) mbar_init(bar(C::kBarX + i), 2);
     fence_barrier_init();
     fence_proxy_async_smem();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
+    // Q does not depend on the tile list: start its load right away.
+    mbar_arrive_expect_tx(bar(C::kBarQ), C::kChunks * 128u * p.R);
+#pragma unroll
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_3d(sQ + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64, kvh * p.G, q_beg + t0);
+    CA_EV(15, 0);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(misc), C::kTmemCols);
     tmem_relinquish();
+    if (lane == 0) CA_EV(15, 1);
   }
   if (warp <= 1)
     build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, t0, p.QT, list, misc, tid);
+  if (tid == 32) CA_EV(15, 2);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (tid == 0) CA_EV(15, 3);
   const uint32_t tmem = static_cast<uint32_t>(misc[0]);
   const int n = misc[1];
   bool dead = false;
@@ -405,12 +429,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t ring = is_k ? sK : sV;
       const int full = is_k ? C::kBarK : C::kBarV;
       const int empty = is_k ? C::kBarKE : C::kBarVE;
-      if (is_k) {
-        mbar_arrive_expect_tx(bar(C::kBarQ), C::kChunks * 128u * p.R);
-#pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sQ + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64, kvh * p.G, q_beg + t0);
-      }
       for (int j = 0; j < n; ++j) {
         const int s = j % ST;
         if (j >= ST && !mbar_wait(bar(empty + s), ((j / ST) - 1) & 1, dead)) break;
@@ -815,6 +833,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogue
+    if ((warp & 3) == 2 && lane == 0) CA_EV(14, 2 + grp);
     // Wait for this group's last P V. kAlt: merge the two groups' (max, sum, O) partials. kSplit: add the two
     // halves' row sums (same running max).
     // kAlt: the merge exchange below borrows the K ring, so wait until every
@@ -914,6 +933,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) CA_EV(14, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);

@@ -166,8 +166,10 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
   p.scale = a->scale;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.softcap = a->softcap > 0.f ? a->softcap : 0.f;
-  p.any_mask = (a->q_pos || a->k_pos || a->q_seq || a->k_seq || a->q_prefix ||
-                p.window != kNoWindow || p.causal_prefix >= 0)
+  // Positions alone mask nothing (visible() reads them only for the window
+  // and the causal prefix), so they do not make a mask by themselves.
+  p.any_mask = (a->q_seq || a->k_seq || a->q_prefix || p.window != kNoWindow ||
+                p.causal_prefix >= 0)
                    ? 1
                    : 0;
 
