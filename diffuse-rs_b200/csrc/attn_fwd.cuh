@@ -89,6 +89,7 @@ struct FwdParams {
   float scale;
   float scale_log2;   // scale * log2(e)
   float softcap;      // 0 = off
+  int tma_out;        // uniform batch: the epilogue stores O through tm_o
   int any_mask;       // any of: seq ids, prefixes, window, causal prefix (positions
                       // alone mask nothing: they matter only to those masks)
 };
@@ -141,11 +142,11 @@ struct FwdCfg {
   // Largest key-tile count per sequence (keys <= kMaxTiles * BN).
   static constexpr int kMaxTiles = 1024;
   static constexpr int kOffList = kOffBar + kNumBars * 8;
-  // Warp-pair exchange, float [parity][half][128]. kAlt uses it once, after
-  // the last P V, in the then idle K ring; kSplit every tile, in its own area.
+  // Warp-pair exchange, float [parity][half][128]: kSplit's per-tile row
+  // maxima and the epilogue's partial (max, sum) of each group.
   static constexpr int kXchBytes = 2 * 2 * 128 * 4;
-  static constexpr int kOffXch = SPLIT ? kOffList + kMaxTiles * 2 : kOffK;
-  static constexpr int kOffMisc = kOffList + kMaxTiles * 2 + (SPLIT ? kXchBytes : 0);
+  static constexpr int kOffXch = kOffList + kMaxTiles * 2;
+  static constexpr int kOffMisc = kOffXch + kXchBytes;
   static constexpr int kMiscBytes = 64;
   static constexpr int kSmemBytes = kOffMisc + kMiscBytes;
   static constexpr int kTmemCols = 512;
@@ -153,9 +154,11 @@ struct FwdCfg {
   static constexpr uint32_t kIdescS = umma_idesc_bf16(128, BN, 0, 0);
   static constexpr uint32_t kIdescO = umma_idesc_bf16(128, HDP, 0, 1);
   static_assert(kOCol + (SPLIT ? 1 : 2) * HDP <= kTmemCols, "TMEM budget");
-  static_assert(SPLIT || ST * kKVBytes >= kXchBytes, "exchange fits in the K ring");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 256, "tile shape");
+  // The epilogue stages the output tile (up to fp32) in the idle K/V rings.
+  static constexpr int kStageChunk = 128 * 128;  // one 128-byte column chunk, 128 rows
+  static_assert(128 * HDP * 4 <= 2 * ST * kKVBytes, "output staging fits in the K/V rings");
 };
 
 // visible(): src/model/attention.rs:35-57 on int32 positions.
@@ -346,7 +349,8 @@ template <class C>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                    const __grid_constant__ CUtensorMap tm_v,
+                    const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
   constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST;
   constexpr bool ALT = C::ALT, SPLIT = C::SPLIT;
   // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
@@ -400,6 +404,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
     for (int c = 0; c < C::kChunks; ++c)
       tma_load_3d(sQ + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64, kvh * p.G, q_beg + t0);
+    // Without masks the visible tiles are 0, 1, 2, ...: the first ring
+    // stages of K and V load now too, overlapping the tile list and the
+    // TMEM allocation (the producers continue from stage ST).
+    if (!p.any_mask) {
+      const int e = min(ST, (k_len + BN - 1) / BN);
+      for (int jj = 0; jj < e; ++jj) {
+        mbar_arrive_expect_tx(bar(C::kBarK + jj), C::kKVBytes);
+        mbar_arrive_expect_tx(bar(C::kBarV + jj), C::kKVBytes);
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c) {
+          tma_load_3d(sK + jj * C::kKVBytes + c * C::kKChunk, &tm_k, bar(C::kBarK + jj), c * 64,
+                      kvh, k_beg + jj * BN);
+          tma_load_3d(sV + jj * C::kKVBytes + c * C::kKChunk, &tm_v, bar(C::kBarV + jj), c * 64,
+                      kvh, k_beg + jj * BN);
+        }
+      }
+    }
     CA_EV(15, 0);
   }
   if (warp == 1) {
@@ -429,7 +450,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t ring = is_k ? sK : sV;
       const int full = is_k ? C::kBarK : C::kBarV;
       const int empty = is_k ? C::kBarKE : C::kBarVE;
-      for (int j = 0; j < n; ++j) {
+      for (int j = p.any_mask ? 0 : min(ST, n); j < n; ++j) {
         const int s = j % ST;
         if (j >= ST && !mbar_wait(bar(empty + s), ((j / ST) - 1) & 1, dead)) break;
         const int krow = k_beg + (list[j] & 0x3fff) * BN;
@@ -836,8 +857,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if ((warp & 3) == 2 && lane == 0) CA_EV(14, 2 + grp);
     // Wait for this group's last P V. kAlt: merge the two groups' (max, sum, O) partials. kSplit: add the two
     // halves' row sums (same running max).
-    // kAlt: the merge exchange below borrows the K ring, so wait until every
-    // MMA is done (also covers a group that had no tile of its own).
+    // kAlt: wait until every MMA is done (the output is staged in the K/V
+    // rings; this also covers a group that had no tile of its own).
     if (ALT && n > 0 && !dead) {
       mbar_wait(bar(C::kBarF), 0, dead);
       dead = __any_sync(0xffffffffu, dead);
@@ -847,12 +868,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       dead = __any_sync(0xffffffffu, dead);
       tc_fence_after();
     }
+    if ((warp & 3) == 2 && lane == 0) CA_EV(14, 4 + grp);
     bool have = n > 0 && !dead;
     float s_me = 1.f, s_ot = 0.f, inv = __int_as_float(0x7fc00000);
     const int n_me = ALT ? (grp == 0 ? (n + 1) / 2 : n / 2) : n;
     const int n_ot = ALT ? (grp == 0 ? n / 2 : (n + 1) / 2) : 0;
     if (have) {
-      // kAlt: [group][l, m][128] in the K ring, idle once every MMA is done.
+      // kAlt: [group][l, m][128].
       float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
       float* xo = ALT ? xch + grp * 256 : xch + ((n & 1) * 2 + grp) * 128;
       float* xp = ALT ? xch + (grp ^ 1) * 256 : xch + ((n & 1) * 2 + (grp ^ 1)) * 128;
@@ -865,6 +887,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       have = !dead;
       tc_fence_after();
       const float l_ot = xp[r];
+      if ((warp & 3) == 2 && lane == 0) CA_EV(14, 6 + grp);
       if (ALT) {
         const float m_ot = xp[128 + r];
         const float mt = fmaxf(n_me > 0 ? m : -INFINITY, n_ot > 0 ? m_ot : -INFINITY);
@@ -903,7 +926,42 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = fmaf(u2f(o[i]), s_ot, v[i]);
       }
-      if (row_valid) {
+      if (p.tma_out) {
+        // Stage row r in 128-byte column chunks, 16-byte units XOR-swizzled
+        // by r & 7 (the tensor map's 128-byte swizzle); rows past the
+        // sequence end and columns past head_dim are clipped by the store.
+        uint8_t* stg = smem + C::kOffK;
+        if (p.out_f32) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int col = col_base + u * 4;
+            const int ci = col >> 5, uu = (col & 31) >> 2;
+            float4 w;
+            w.x = have ? v[u * 4] * inv : inv;
+            w.y = have ? v[u * 4 + 1] * inv : inv;
+            w.z = have ? v[u * 4 + 2] * inv : inv;
+            w.w = have ? v[u * 4 + 3] * inv : inv;
+            *reinterpret_cast<float4*>(stg + ci * C::kStageChunk + r * 128 +
+                                       ((uu ^ (r & 7)) << 4)) = w;
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int col = col_base + u * 8;
+            const int ci = col >> 6, uu = (col & 63) >> 3;
+            float w8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w8[i] = have ? v[u * 8 + i] * inv : inv;
+            uint4 w;
+            w.x = pack_bf16(w8[0], w8[1]);
+            w.y = pack_bf16(w8[2], w8[3]);
+            w.z = pack_bf16(w8[4], w8[5]);
+            w.w = pack_bf16(w8[6], w8[7]);
+            *reinterpret_cast<uint4*>(stg + ci * C::kStageChunk + r * 128 +
+                                      ((uu ^ (r & 7)) << 4)) = w;
+          }
+        }
+      } else if (row_valid) {
         const int64_t obase = static_cast<int64_t>(gq) * p.out_row_stride +
                               static_cast<int64_t>(head) * p.hd;
 #pragma unroll
@@ -929,6 +987,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
     }
+    if (p.tma_out) {
+      // All softmax warps have staged their rows: one thread stores the tile.
+      fence_proxy_async_smem();
+      named_bar_sync(2, 256);
+      if (warp == 3 && lane == 0) {
+        const int inner = p.out_f32 ? 32 : 64;  // elements per 128-byte chunk
+        for (int ci = 0; ci * inner < p.hd; ++ci)
+          tma_store_4d(&tm_o, smem_u32(smem + C::kOffK + ci * C::kStageChunk), ci * inner,
+                       kvh * p.G, t0, b);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+      }
+    }
+    if ((warp & 3) == 2 && lane == 0) CA_EV(14, 8 + grp);
   }
 
   tc_fence_before();

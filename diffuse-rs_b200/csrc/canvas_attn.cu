@@ -58,6 +58,31 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t hd, int64_t heads, int64
   return r == CUDA_SUCCESS ? CA_OK : CA_ERR_INVALID;
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 4-D view of the output [batch][tokens][heads][hd] (uniform batch), bf16 or
+// fp32, boxes of one 128-byte column chunk x box_heads x box_tokens, 128-byte
+// swizzle. Stores clip at each sequence's end and at head_dim.
+int make_tmap_out(CUtensorMap* m, void* base, int64_t hd, int64_t heads, int64_t sq,
+                  int64_t batch, int64_t row_stride_elems, bool f32, uint32_t box_heads,
+                  uint32_t box_tokens) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return CA_ERR_CUDA;
+  const uint64_t es = f32 ? 4 : 2;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(sq), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(hd) * es,
+                           static_cast<cuuint64_t>(row_stride_elems) * es,
+                           static_cast<cuuint64_t>(row_stride_elems * sq) * es};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), box_heads, box_tokens, 1};
+  cuuint32_t elem[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                  base, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CA_OK : CA_ERR_INVALID;
+}
+
 // ---------------------------------------------------------------- launch
 // Builds the tensor maps for one tile configuration and launches it.
 struct Launch {
@@ -74,13 +99,24 @@ struct Launch {
     static bool attr_done[kMaxDevices] = {};
     const int64_t n_kt = (max_sk + C::BN - 1) / C::BN;
     if (n_kt > C::kMaxTiles) return CA_ERR_UNSUPPORTED;
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tq, tk, tv, to;
     const int hd = p->hd;
     const int64_t tk_rows = total_k == 0 ? 1 : total_k;
     int rc;
     if ((rc = make_tmap(&tq, a->q, hd, p->n_head, total_q, qrs, p->G, p->QT)) != CA_OK) return rc;
     if ((rc = make_tmap(&tk, a->k, hd, p->n_head_kv, tk_rows, krs, 1, C::BN)) != CA_OK) return rc;
     if ((rc = make_tmap(&tv, a->v, hd, p->n_head_kv, tk_rows, krs, 1, C::BN)) != CA_OK) return rc;
+    // Uniform batches store O through a tensor map (the map clips at each
+    // sequence's end); otherwise the kernel stores rows itself.
+    FwdParams pl = *p;
+    const int64_t es = p->out_f32 ? 4 : 2;
+    pl.tma_out = !a->cu_q && p->batch > 0 && p->sq > 0 && aligned16(a->out) &&
+                 (p->out_row_stride * es) % 16 == 0 && (p->hd * es) % 16 == 0;
+    if (pl.tma_out &&
+        make_tmap_out(&to, a->out, hd, p->n_head, p->sq, p->batch, p->out_row_stride,
+                      p->out_f32 != 0, p->G, p->QT) != CA_OK)
+      pl.tma_out = 0;
+    if (!pl.tma_out) to = tq;  // unused
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
     if (!attr_done[dev]) {
@@ -91,12 +127,11 @@ struct Launch {
     }
     const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
     dim3 grid(n_qtiles, p->n_head_kv, p->batch);
-    attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, *p);
+    attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, to, pl);
     return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
   }
 };
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int clamp_opt(int64_t v) {  // Option<usize> as int32 (None = -1)
   if (v < 0) return -1;
@@ -177,18 +212,19 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
   // One Q tile per CTA. head_dim <= 192: the two softmax groups alternate
   // key tiles (kAlt). head_dim 256: they split every tile's key columns
   // around one O, with three S buffers (kSplit). P lives in TMEM, so shared
-  // memory holds only Q and the K/V rings; ring depths fill what is left of
-  // 227 KB. (kSplit with three S buffers at head_dim 128 measured 746 vs
-  // 823 TFLOP/s for kAlt at B8 S4096 H16.)
+  // memory holds only Q and the K/V rings. Two stages measured faster than
+  // three at head_dim 128 (970 vs 949 TFLOP/s at B8 S4096 H16; the smaller
+  // shared-memory carve-out leaves more L1), and at head_dim 64 and 192. (kSplit with three S buffers
+  // at head_dim 128 measured 746 vs 823 TFLOP/s for kAlt.)
   if (a->precise) {
-    if (hdp == 64) return L.run<FwdCfg<64, 128, 4, true, kAlt>>();
-    if (hdp == 128) return L.run<FwdCfg<128, 128, 3, true, kAlt>>();
-    if (hdp == 192) return L.run<FwdCfg<192, 64, 3, true, kAlt>>();
+    if (hdp == 64) return L.run<FwdCfg<64, 128, 2, true, kAlt>>();
+    if (hdp == 128) return L.run<FwdCfg<128, 128, 2, true, kAlt>>();
+    if (hdp == 192) return L.run<FwdCfg<192, 64, 2, true, kAlt>>();
     return L.run<FwdCfg<256, 64, 2, true, kSplit>>();
   }
-  if (hdp == 64) return L.run<FwdCfg<64, 128, 4, false, kAlt>>();
-  if (hdp == 128) return L.run<FwdCfg<128, 128, 3, false, kAlt>>();
-  if (hdp == 192) return L.run<FwdCfg<192, 64, 3, false, kAlt>>();
+  if (hdp == 64) return L.run<FwdCfg<64, 128, 2, false, kAlt>>();
+  if (hdp == 128) return L.run<FwdCfg<128, 128, 2, false, kAlt>>();
+  if (hdp == 192) return L.run<FwdCfg<192, 64, 2, false, kAlt>>();
   return L.run<FwdCfg<256, 64, 2, false, kSplit>>();
 }
 
