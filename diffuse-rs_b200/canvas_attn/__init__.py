@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "ca_attention_block_dev_noalloc",
     "ca_build_rope_table",
     "ca_device_status",
+    "ca_selftest_wait_timeout",
     "ca_status_string",
     "ca_version",
 )
@@ -117,6 +118,8 @@ def _load():
     L.ca_build_rope_table.restype = ctypes.c_int
     L.ca_device_status.argtypes = [ctypes.c_void_p]
     L.ca_device_status.restype = ctypes.c_int
+    L.ca_selftest_wait_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p]
+    L.ca_selftest_wait_timeout.restype = ctypes.c_int
     L.ca_status_string.argtypes = [ctypes.c_int]
     L.ca_status_string.restype = ctypes.c_char_p
     L.ca_version.restype = ctypes.c_char_p
@@ -299,3 +302,11 @@ def build_rope_cache(max_seq_len: int, rope_dim: int, theta: float,
 def device_status(stream=None) -> int:
     """Synchronises `stream`, then reads and clears the device error word."""
     return int(lib.ca_device_status(_stream(stream)))
+
+
+def selftest_wait_timeout(limit_ns: int, stream=None) -> None:
+    """Launches the failure-detection self-test: a wait on an mbarrier that
+    nothing arrives on, bounded by `limit_ns`. Returns once launched; the
+    expiry shows up in the next device_status() as CA_ERR_TIMEOUT."""
+    _check(lib.ca_selftest_wait_timeout(int(limit_ns), _stream(stream)),
+           "ca_selftest_wait_timeout")

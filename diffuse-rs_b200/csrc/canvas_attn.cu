@@ -507,10 +507,35 @@ int noalloc_impl(const ca_block_args* a, cudaStream_t st) {
   return block_impl(&b, st);
 }
 
+// Failure-detection self-test: one CTA waits on an mbarrier that nothing
+// arrives on, through the same bounded wait (mbar_wait_limit) every pipeline
+// wait in the attention kernel uses, with a caller-chosen limit. The wait
+// gives up, stores CA_ERR_TIMEOUT in the device error word and the kernel
+// returns normally: the host sees the expiry through ca_device_status and
+// the context stays usable. No trap, fault or unbounded loop is involved.
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t never;
+  const uint32_t bar = smem_u32(&never);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  bool dead = false;
+  mbar_wait_limit(bar, 0, dead, limit_ns);
+}
+
 }  // namespace
 }  // namespace ca
 
 extern "C" {
+
+int ca_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0 || limit_ns > 1000000000ll) return CA_ERR_INVALID;
+  ca::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint64_t>(limit_ns));
+  return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
+}
 
 int ca_attention_block_dev_noalloc(const ca_block_args* a, void* stream) {
   return ca::noalloc_impl(a, static_cast<cudaStream_t>(stream));

@@ -83,18 +83,23 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 // Waits for the phase with the given parity to complete. Returns false (and
 // records the timeout in g_device_error) if it does not complete within
 // kWaitLimitNs, or immediately if *dead is already set by an earlier expiry.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, bool& dead) {
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, bool& dead,
+                                                uint64_t limit_ns) {
   if (dead) return false;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (!mbar_try_wait_sleep(bar, parity, 100000u)) {
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       atomicExch(&g_device_error, kErrTimeout);
       dead = true;
       return false;
     }
   }
   return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, bool& dead) {
+  return mbar_wait_limit(bar, parity, dead, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------- TMA

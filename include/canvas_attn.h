@@ -208,6 +208,18 @@ int ca_build_rope_table(float* out, int64_t max_seq_len, int64_t rope_dim, float
  * expired since the last call. */
 int ca_device_status(void* stream);
 
+/*
+ * ca_selftest_wait_timeout -- failure-detection self-test, no counterpart in
+ * the reference (whose CPU path has no device waits). Launches one CTA on
+ * `stream` that waits on an mbarrier nothing arrives on, through the same
+ * bounded wait every pipeline wait of the attention kernel uses, giving up
+ * after `limit_ns` nanoseconds (1 ns .. 1 s). The kernel returns normally;
+ * a following ca_device_status(stream) returns CA_ERR_TIMEOUT once and then
+ * CA_OK, and the CUDA context stays usable. Lets a host verify on its own
+ * GPU that an expired wait is reported instead of hanging.
+ */
+int ca_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
 /* Human-readable text of a ca_status. */
 const char* ca_status_string(int status);
 

@@ -86,3 +86,9 @@ def test_host_entry_validates_shape():
                                       k.ctypes.data, ctypes.byref(cs), ctypes.byref(cq),
                                       ctypes.byref(ck))
     assert rc == ca.CA_ERR_INVALID
+
+
+def test_selftest_rejects_bad_limits_without_launching():
+    assert ca.lib.ca_selftest_wait_timeout(0, None) == ca.CA_ERR_INVALID
+    assert ca.lib.ca_selftest_wait_timeout(-5, None) == ca.CA_ERR_INVALID
+    assert ca.lib.ca_selftest_wait_timeout(2_000_000_000, None) == ca.CA_ERR_INVALID
