@@ -280,38 +280,44 @@ class CpuSample:
         return min(self.cfg["n_total"] - 1, qpos + window - 1) - max(0, qpos - window + 1) + 1
 
     def run(self, n_rows):
-        """Runs about n_rows rows spread over every layer; returns (flops, seconds)."""
+        """Runs about n_rows rows spread over every layer, repeating whole
+        layers when n_rows exceeds them; returns (flops, seconds, rows run)."""
         np, c = self.np, self.cfg
         n_tasks = c["H"] * c["na"]
         per_layer = max(1, n_rows // len(c["layers"]))
-        flops, secs = 0.0, 0.0
+        reps = max(1, per_layer // n_tasks)
+        flops, secs, rows = 0.0, 0.0, 0
         for window, _theta in c["layers"]:
             tasks = np.unique(np.linspace(0, n_tasks - 1, min(per_layer, n_tasks)).astype(np.int64))
             qrows = tasks % c["na"]
-            flops += 4.0 * c["hd"] * sum(self.row_visible(int(self.q_pos[r]), window)
-                                         for r in qrows)
+            flops += reps * 4.0 * c["hd"] * sum(self.row_visible(int(self.q_pos[r]), window)
+                                                for r in qrows)
+            rows += reps * len(tasks)
             t0 = time.perf_counter()
-            self.orc.attention(self.q, self.k, self.v, nq=c["na"], nk=c["n_total"],
-                               n_head=c["H"], n_head_kv=c["Hkv"], head_dim=c["hd"],
-                               q_pos=self.q_pos, k_pos=self.k_pos, sliding_window=window,
-                               scale=c["scale"], softcap=c["softcap"], kind=self.kind,
-                               threads=self.threads, tasks=tasks, out=self.out)
+            for _ in range(reps):
+                self.orc.attention(self.q, self.k, self.v, nq=c["na"], nk=c["n_total"],
+                                   n_head=c["H"], n_head_kv=c["Hkv"], head_dim=c["hd"],
+                                   q_pos=self.q_pos, k_pos=self.k_pos, sliding_window=window,
+                                   scale=c["scale"], softcap=c["softcap"], kind=self.kind,
+                                   threads=self.threads, tasks=tasks, out=self.out)
             secs += time.perf_counter() - t0
-        return flops, secs
+        return flops, secs, rows
 
     def calibrate(self, target_s):
+        """Row count whose run takes about target_s seconds."""
         n = 64 * len(self.cfg["layers"])
         self.run(n)  # thread-pool start-up
-        for _ in range(3):  # grow the probe until it takes ~0.5 s
-            f, s = self.run(n)
-            if s > 0.5:
+        for _ in range(6):  # grow the probe until it takes ~1/4 of the target
+            _f, s, rows = self.run(n)
+            if s > min(0.5, target_s / 4):
                 break
-            n = int(n * min(16.0, 0.6 / max(s, 1e-4)))
-        return max(16, int(n / max(s, 1e-6) * target_s))
+            n = int(rows * min(16.0, 0.6 / max(s, 1e-4)))
+        return max(16, int(rows / max(s, 1e-6) * target_s))
 
-    def describe(self, n_rows, config):
-        return (f"{n_rows} (head, query) rows of one {config} sequence spread over "
-                f"{len(self.cfg['layers'])} layer(s), {self.cfg['n_total']} keys each")
+    def describe(self, rows, config):
+        return (f"{rows} (head, query) rows of the {config} config (one sequence, repeated "
+                f"when the sample exceeds it) over {len(self.cfg['layers'])} layer(s), "
+                f"{self.cfg['n_total']} keys each")
 
 
 class E2E:
@@ -491,9 +497,9 @@ def run_ours(args, cfg):
     if rank == 0 and world == 1 and not args.no_cpu:
         cs = CpuSample(cfg)
         n_rows = cs.calibrate(args.cpu_seconds)
-        f, s = cs.run(n_rows)
+        f, s, rows = cs.run(n_rows)
         cpu = dict(value=f / s / 1e12, unit="TFLOP/s", cores=cs.threads, kind="port",
-                   sample=cs.describe(n_rows, args.config) + f", {s:.1f} s")
+                   sample=cs.describe(rows, args.config) + f", {s:.1f} s")
 
     if rank == 0:
         line = {
@@ -541,13 +547,14 @@ def run_reference(args, cfg):
     n_rows = cs.calibrate(args.ref_step_seconds)
     for _ in range(args.warmup):
         cs.run(max(16, n_rows // 8))
-    tf, ts = 0.0, 0.0
+    tf, ts, tr = 0.0, 0.0, 0
     for _ in range(args.steps):
-        f, s = cs.run(n_rows)
+        f, s, rows = cs.run(n_rows)
         tf += f
         ts += s
+        tr += rows
     value = tf / ts / 1e12
-    sample = cs.describe(n_rows, args.config) + " per step"
+    sample = cs.describe(tr // max(1, args.steps), args.config) + " per step"
     line = {
         "impl": "reference",
         "metric": "canvas-attention TFLOP/s",
