@@ -274,7 +274,10 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
     const long long toks = static_cast<long long>(a->batch) * a->n_active;
     const long long pjobs = toks * ((H + 2 * Hkv + 15) / 16);
     const int blocks = static_cast<int>(std::min<long long>((pjobs + 7) / 8, 148LL * 8));
-    if (hd == 64) prep_token_kernel<8><<<blocks, 256, 0, st>>>(pp);
+    // head_dim 256 with full rotation: every NeoX pair inside one lane
+    // (measured faster there; at 64 / 128 the partner-exchange form is).
+    if (hd == 256 && a->rope_dim == hd) prep_pair_kernel<32><<<blocks, 256, 0, st>>>(pp);
+    else if (hd == 64) prep_token_kernel<8><<<blocks, 256, 0, st>>>(pp);
     else if (hd == 128) prep_token_kernel<16><<<blocks, 256, 0, st>>>(pp);
     else prep_token_kernel<32><<<blocks, 256, 0, st>>>(pp);
   } else {

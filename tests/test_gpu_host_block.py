@@ -95,9 +95,13 @@ def _oracle_block(q, k, v, pos, wq, wk, rope, rope_dim, h, hkv, hd, eps):
     return rb(q), rb(k), v
 
 
-@pytest.mark.parametrize("qk_norm", [False, True])
-def test_block_without_cache(qk_norm):
-    B, S, H, Hkv, hd = 2, 300, 4, 4, 128
+@pytest.mark.parametrize("qk_norm,hd,rope_dim,hkv", [
+    (False, 128, 128, 4), (True, 128, 128, 4),
+    (True, 64, 64, 2), (True, 256, 256, 2),       # 256: lane-paired pre-ops
+    (True, 128, 64, 4),                           # partial rotation
+])
+def test_block_without_cache(qk_norm, hd, rope_dim, hkv):
+    B, S, H, Hkv = 2, 300, 4, hkv
     eps, theta = 1e-6, 50000.0
     g = torch.Generator().manual_seed(31)
     q = bf16_round(randn(g, B, S, H, hd))
@@ -105,7 +109,7 @@ def test_block_without_cache(qk_norm):
     v = bf16_round(randn(g, B, S, Hkv, hd))
     wq = torch.rand(hd, generator=g) + 0.5 if qk_norm else None
     wk = torch.rand(hd, generator=g) + 0.5 if qk_norm else None
-    rope = ca.build_rope_cache(4096, hd, theta)
+    rope = ca.build_rope_cache(4096, rope_dim, theta)
     pos = torch.arange(S, dtype=torch.int32).repeat(B, 1)
     dev = dict(q=q.to(torch.bfloat16).cuda(), k=k.to(torch.bfloat16).cuda(),
                v=v.to(torch.bfloat16).cuda())
@@ -115,7 +119,8 @@ def test_block_without_cache(qk_norm):
     out = torch.empty(B, S, H, hd, device="cuda")
     rope_d = torch.from_numpy(rope).cuda()
     ca.attention_block_dev(dev["q"], dev["k"], dev["v"], batch=B, n_active=S,
-                           active_pos=pos.cuda(), rope=rope_d, rope_len=4096, rope_dim=hd,
+                           active_pos=pos.cuda(), rope=rope_d, rope_len=4096,
+                           rope_dim=rope_dim,
                            cache_k=cache_k, cache_v=cache_v, n_total=S, q_work=q_work, out=out,
                            n_head=H, n_head_kv=Hkv, head_dim=hd,
                            q_norm_w=None if wq is None else wq.cuda(),
@@ -127,12 +132,12 @@ def test_block_without_cache(qk_norm):
         qq, kk, vv = _oracle_block(q[b].numpy().reshape(-1), k[b].numpy().reshape(-1),
                                    v[b].numpy().reshape(-1), np.arange(S), None if wq is None
                                    else wq.numpy(), None if wk is None else wk.numpy(), rope,
-                                   hd, H, Hkv, hd, eps)
+                                   rope_dim, H, Hkv, hd, eps)
         # The stored cache holds bf16 post-RoPE K (the GPU's operand).
         kc = cache_k[b].float().cpu().numpy().reshape(-1)
         np.testing.assert_allclose(kc, kk, atol=1e-2, rtol=1e-2)
         ref = oracle_attention(qq, kk, vv, nq=S, nk=S, h=H, hkv=Hkv, hd=hd, scale=hd ** -0.5)
-        check_close(got[b], ref, H, hd, what=f"block qk_norm={qk_norm} b={b}")
+        check_close(got[b], ref, H, hd, what=f"block qk_norm={qk_norm} hd={hd} rope_dim={rope_dim} b={b}")
 
 
 def test_block_with_cache_reuse_over_steps():
