@@ -173,6 +173,24 @@ __device__ __forceinline__ bool visible_dev(int qpos, int kpos, int qseq, int ks
   return true;
 }
 
+// Blackwell packed / three-input forms for the softmax inner loops
+// (sm_100: fma.rn.f32x2 / add.f32x2 through __ffma2_rn / __fadd2_rn, and the
+// three-operand max.f32 of PTX 8.8).
+#ifndef CA_F32X2
+#define CA_F32X2 1
+#endif
+#ifndef CA_MAX3
+#define CA_MAX3 1
+#endif
+#ifndef CA_TANH2
+#define CA_TANH2 1
+#endif
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
 
@@ -204,6 +222,18 @@ __device__ __forceinline__ float tanh_poly(float u) {
   p = fmaf(p, w, kTanhC1);
   p = fmaf(p, w, 1.f);
   return u * p;
+}
+
+// tanh_poly on two values at once with packed f32x2 FMAs (same operations
+// in the same order, so the same results as two tanh_poly calls).
+__device__ __forceinline__ float2 tanh_poly2(float2 u) {
+  const float2 w = __fmul2_rn(u, u);
+  float2 p = __ffma2_rn(make_float2(kTanhC5, kTanhC5), w, make_float2(kTanhC4, kTanhC4));
+  p = __ffma2_rn(p, w, make_float2(kTanhC3, kTanhC3));
+  p = __ffma2_rn(p, w, make_float2(kTanhC2, kTanhC2));
+  p = __ffma2_rn(p, w, make_float2(kTanhC1, kTanhC1));
+  p = __ffma2_rn(p, w, make_float2(1.f, 1.f));
+  return __fmul2_rn(u, p);
 }
 
 }  // namespace ca
@@ -691,8 +721,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               const float x = V == kPlain ? u2f(sr[i]) : sgn * u2f(sr[i]);
               v[i] = vis(msk_c, cb * LB + i) ? x : -INFINITY;
             }
+#if CA_MAX3
+#pragma unroll
+            for (int i = 0; i < LB; i += 2) mx8[(i >> 1) & 7] = fmax3(mx8[(i >> 1) & 7], v[i], v[i + 1]);
+#else
 #pragma unroll
             for (int i = 0; i < LB; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], v[i]);
+#endif
             if constexpr (V == kCap) {
 #pragma unroll
               for (int i = 0; i < LB; ++i)
@@ -755,8 +790,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // and (PRECISE) of the lo terms in the last 8. Every block lands inside
       // the columns it was read from, so no unread S is overwritten.
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#if CA_F32X2
+      float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#endif
       auto emit = [&](float p0, float p1, int q2, uint32_t& hi, uint32_t& lo) {
+#if CA_F32X2
+        sum2[q2 & 1] = __fadd2_rn(sum2[q2 & 1], make_float2(p0, p1));
+#else
         sum4[q2 & 3] += p0 + p1;
+#endif
         hi = pack_bf16(p0, p1);
         if constexpr (C::PRECISE) {
           const float h0 = __uint_as_float(hi << 16);
@@ -796,11 +838,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                   x0 = logit_nm(sr[i]) - mu;
                   x1 = logit_nm(sr[i + 1]) - mu;
                 } else if constexpr (V == kCapPoly) {
-                  x0 = fmaf(cap_l2, tanh_poly(u2f(sr[i]) * scale_cap), -mu);
-                  x1 = fmaf(cap_l2, tanh_poly(u2f(sr[i + 1]) * scale_cap), -mu);
+                  // Packed form only in the head_dim 256 (kSplit) kernel: it
+                  // measured +4% on soft-capped layers there, but -1.3% on
+                  // the head_dim 128 kernel's uncapped tiles (code layout).
+                  if constexpr (SPLIT && CA_TANH2) {
+                    const float2 t = tanh_poly2(__fmul2_rn(
+                        make_float2(u2f(sr[i]), u2f(sr[i + 1])), make_float2(scale_cap, scale_cap)));
+                    const float2 x01 = __ffma2_rn(make_float2(cap_l2, cap_l2), t,
+                                                  make_float2(-mu, -mu));
+                    x0 = x01.x;
+                    x1 = x01.y;
+                  } else {
+                    x0 = fmaf(cap_l2, tanh_poly(u2f(sr[i]) * scale_cap), -mu);
+                    x1 = fmaf(cap_l2, tanh_poly(u2f(sr[i + 1]) * scale_cap), -mu);
+                  }
                 } else {
+#if CA_F32X2
+                  const float2 x01 = __ffma2_rn(make_float2(u2f(sr[i]), u2f(sr[i + 1])),
+                                                make_float2(sl2, sl2), make_float2(-mu, -mu));
+                  x0 = x01.x;
+                  x1 = x01.y;
+#else
                   x0 = fmaf(u2f(sr[i]), sl2, -mu);
                   x1 = fmaf(u2f(sr[i + 1]), sl2, -mu);
+#endif
                 }
                 if constexpr (M != kNone) {
                   x0 = vis(msk_c, cb * LB + i) ? x0 : -INFINITY;
@@ -815,6 +876,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         };
         dispatch(pass2);
       }
+#if CA_F32X2
+      sum4[0] += sum2[0].x;
+      sum4[1] += sum2[0].y;
+      sum4[2] += sum2[1].x;
+      sum4[3] += sum2[1].y;
+#endif
       l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
       if ((warp & 3) == 2 && lane == 0) CA_EV(8, j);
       CA_EVW(2, j);
