@@ -21,6 +21,9 @@ Configs (seeded N(0,1) bf16 inputs):
 Default workload: c3, the 4k-token bidirectional case the north-star target
 names. Multi-GPU is weak scaling: every rank runs its own full batch of the
 config (sequences are independent, so no collective is on the data path).
+Under torchrun the line also carries `head_sharded`: the same global batch
+split by kv heads over the ranks plus one NCCL all-gather per layer of the
+head slices (strong scaling, compute only and with the gather).
 
 Metric: TFLOP/s = 4 * head_dim * visible (query, key) pairs * n_head summed
 over the batch and layers, divided by time (softmax, RoPE and norms excluded).
@@ -378,7 +381,20 @@ def dist_setup(want_gpus):
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # NCCL prints a version banner on stdout while the communicator is
+        # created (eagerly here, device_id given); keep stdout for the one
+        # JSON line by pointing file descriptor 1 at stderr meanwhile.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     if want_gpus != world and rank == 0:
         print(f"note: --gpus {want_gpus} but WORLD_SIZE {world}; using {world}", file=sys.stderr)
     return world, rank, local
@@ -407,6 +423,44 @@ def physical_gpu_index(local):
         if local < len(ids) and ids[local].isdigit():
             return int(ids[local])
     return local
+
+
+def run_head_sharded(args, cfg, world, dev):
+    import torch
+    from canvas_attn.sharding import gather_heads
+    local = dict(cfg, H=cfg["H"] // world, Hkv=cfg["Hkv"] // world)
+    wl = Workload(local, dev, seed=4321 + int(os.environ.get("RANK", "0")))
+    tok = cfg["B"] * cfg["na"]
+
+    def gather_all():
+        return [gather_heads(L["out"].view(tok, local["H"], cfg["hd"])) for L in wl.layers]
+
+    for i in range(args.warmup):
+        wl.step(i)
+        gather_all()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        ev[i][0].record(wl.stream)
+        wl.step(i)
+        ev[i][1].record(wl.stream)
+        full = gather_all()
+        ev[i][2].record(wl.stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    assert full[0].shape == (tok, cfg["H"], cfg["hd"])
+    comp = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in ev), world)
+    tot = max_over_ranks(sum(a.elapsed_time(c) for a, _, c in ev), world)
+    flops = step_flops(cfg) * args.steps
+    return dict(value=round(flops / (tot * 1e-3) / 1e12, 2), unit="TFLOP/s",
+                compute_only=round(flops / (comp * 1e-3) / 1e12, 2),
+                ms_per_step=round(tot / args.steps, 4),
+                gather_ms_per_step=round((tot - comp) / args.steps, 4),
+                heads_per_rank=local["H"], kv_heads_per_rank=local["Hkv"],
+                global_batch=cfg["B"], scaling="strong",
+                collective="one NCCL all_gather_into_tensor per layer")
 
 
 def run_ours(args, cfg):
@@ -477,6 +531,15 @@ def run_ours(args, cfg):
     roof["traffic"] = load_traffic(args.config)
     roof["kernel_ms"] = round(attn_ms, 4)
 
+    # Head sharding (N > 1): every rank computes its kv-head slice (and the
+    # query heads of those groups) of ONE global batch of the config, then
+    # one NCCL all-gather per layer reassembles full [tokens, n_head, hd]
+    # rows for o_proj (src/model/forward.rs:345). Strong scaling; reported
+    # compute-only and with the gather, both max over ranks.
+    head_sharded = None
+    if world > 1 and cfg["Hkv"] % world == 0 and not args.no_head_shard:
+        head_sharded = run_head_sharded(args, cfg, world, dev)
+
     # End to end through the host-buffer drop-in entry point.
     e2e = None
     if not args.no_e2e:
@@ -525,6 +588,7 @@ def run_ours(args, cfg):
                        else "inputs larger than L2, no flush",
                        "parallelism": f"dp{world} (independent sequences per rank)"},
             "roofline": roof,
+            "head_sharded": head_sharded,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": wl.launches_per_step * args.steps,
@@ -590,6 +654,8 @@ def main():
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-head-shard", action="store_true",
+                    help="skip the head-sharded (all-gather) leg under torchrun")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

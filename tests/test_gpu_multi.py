@@ -1,0 +1,90 @@
+"""Head sharding across two GPUs with NCCL (skipped with fewer than 2 GPUs).
+
+Each rank runs the fused attention block on its own kv heads (and their
+query heads) of the same seeded batch, then one NCCL all-gather reassembles
+[tokens, n_head, head_dim] rows, the layout o_proj consumes
+(src/model/forward.rs:345). A kv head's work does not depend on the other
+heads, so the gathered result must equal a single-GPU run bit for bit."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+B, S, H, HKV, HD = 2, 640, 8, 4, 128
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(77)
+    q = torch.randn(B, S, H, HD, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, S, HKV, HD, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, S, HKV, HD, generator=g).to(torch.bfloat16)
+    wq = torch.rand(HD, generator=g) + 0.5
+    wk = torch.rand(HD, generator=g) + 0.5
+    return q, k, v, wq, wk
+
+
+def _block(q, k, v, wq, wk, h, hkv, dev):
+    import canvas_attn as ca
+    rope = torch.from_numpy(ca.build_rope_cache(4096, HD, 5e4)).to(dev)
+    pos = torch.arange(S, dtype=torch.int32, device=dev).repeat(B, 1).contiguous()
+    cache_k = torch.zeros(B, S, hkv, HD, dtype=torch.bfloat16, device=dev)
+    cache_v = torch.zeros_like(cache_k)
+    q_work = torch.empty(B, S, h, HD, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(B, S, h, HD, dtype=torch.bfloat16, device=dev)
+    ca.attention_block_dev(q.contiguous().to(dev), k.contiguous().to(dev),
+                           v.contiguous().to(dev), batch=B, n_active=S, active_pos=pos,
+                           rope=rope, rope_len=4096, rope_dim=HD, cache_k=cache_k,
+                           cache_v=cache_v, n_total=S, q_work=q_work, out=out, n_head=h,
+                           n_head_kv=hkv, head_dim=HD, q_norm_w=wq.to(dev), k_norm_w=wk.to(dev),
+                           rms_eps=1e-6, scale=HD ** -0.5)
+    return out
+
+
+def _worker(rank, world, port, result_path):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    sys.path[:0] = [os.path.join(root, "diffuse-rs_b200"), root]
+    import torch.distributed as dist
+    import canvas_attn as ca
+    from canvas_attn.sharding import gather_heads, head_shard
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        q, k, v, wq, wk = _inputs()
+        sh = head_shard(H, HKV, world, rank)
+        out = _block(q[:, :, sh.q_begin:sh.q_end], k[:, :, sh.kv_begin:sh.kv_end],
+                     v[:, :, sh.kv_begin:sh.kv_end], wq, wk, sh.q_end - sh.q_begin,
+                     sh.kv_end - sh.kv_begin, dev)
+        full = gather_heads(out.view(B * S, sh.q_end - sh.q_begin, HD))
+        torch.cuda.synchronize()
+        assert ca.device_status() == ca.CA_OK
+        if rank == 0:
+            ref = _block(q, k, v, wq, wk, H, HKV, dev).view(B * S, H, HD)
+            torch.cuda.synchronize()
+            ok = torch.equal(full, ref)
+            diff = (full.float() - ref.float()).abs().max().item()
+            with open(result_path, "w") as f:
+                f.write(f"{int(ok)} {diff}\n")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_head_sharded_block_with_nccl_gather_matches_one_gpu(tmp_path):
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    res = tmp_path / "result.txt"
+    mp.spawn(_worker, args=(2, port, str(res)), nprocs=2, join=True)
+    ok, diff = res.read_text().split()
+    assert ok == "1", f"gathered head-sharded output differs (max abs diff {diff})"
