@@ -309,9 +309,13 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
 
 // Library-owned device buffers of the host-buffer entry point, one set per
 // device, grown on demand and kept for the process lifetime.
+constexpr int kMaxChunks = 8;
 struct HostCtx {
   std::mutex mu;
-  cudaStream_t stream = nullptr;
+  cudaStream_t stream = nullptr;  // copies in
+  cudaStream_t comp = nullptr;    // conversions + attention (pipelined calls)
+  cudaStream_t outs = nullptr;    // copies out (pipelined calls)
+  cudaEvent_t ev[2 * kMaxChunks + 1] = {};
   void* buf = nullptr;
   size_t cap = 0;
 };
@@ -399,6 +403,101 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
   int32_t* dmeta = reinterpret_cast<int32_t*>(carve(b_meta));
   int32_t* dzero = dmeta + meta.size();
   cudaStream_t st = c.stream;
+  // Large calls without head_dim padding run as a pipeline over chunks of
+  // query rows on three streams: K, V and the row metadata are copied in
+  // first; then per chunk the Q rows are copied in (stream `stream`),
+  // converted and attended over all keys (`comp`), and the output rows are
+  // copied out (`outs`) while later chunks are still arriving. Rows are
+  // independent (attention.rs:116), so the results equal the one-shot form.
+  const int64_t q_bytes = qe * 4;
+  const int n_chunks =
+      (hd_p == hd && nk > 0 && q_bytes >= (16ll << 20))
+          ? static_cast<int>(std::min<int64_t>(kMaxChunks, std::max<int64_t>(2, q_bytes >> 23)))
+          : 1;
+  if (n_chunks > 1) {
+    // On an error, drain what was queued so the next call cannot overlap it.
+    auto fail = [&](int rc) {
+      cudaStreamSynchronize(st);
+      if (c.comp) cudaStreamSynchronize(c.comp);
+      if (c.outs) cudaStreamSynchronize(c.outs);
+      return rc;
+    };
+    if (!c.comp && cudaStreamCreateWithFlags(&c.comp, cudaStreamNonBlocking) != cudaSuccess)
+      return CA_ERR_CUDA;
+    if (!c.outs && cudaStreamCreateWithFlags(&c.outs, cudaStreamNonBlocking) != cudaSuccess)
+      return CA_ERR_CUDA;
+    for (auto& e : c.ev)
+      if (!e && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+        return CA_ERR_CUDA;
+    const int64_t row_e = s->n_head * hd;  // elements per query row
+    const int64_t rows_per = (nq + n_chunks - 1) / n_chunks;
+    bool okp = cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+               cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+               cudaMemcpyAsync(dmeta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice,
+                               st) == cudaSuccess;
+    if (okp && qseq != kseq) okp = cudaMemsetAsync(dzero, 0, 4 * (nq + nk), st) == cudaSuccess;
+    okp = okp && cudaEventRecord(c.ev[2 * kMaxChunks], st) == cudaSuccess &&
+          cudaStreamWaitEvent(c.comp, c.ev[2 * kMaxChunks], 0) == cudaSuccess;
+    if (!okp) return fail(CA_ERR_CUDA);
+    const int kblocks = static_cast<int>(std::min<long long>((ke / 4 + 255) / 256 + 1, 148 * 8));
+    f32_to_bf16_kernel<<<kblocks, 256, 0, c.comp>>>(dk, hk, ke);
+    f32_to_bf16_kernel<<<kblocks, 256, 0, c.comp>>>(dv, hv, ke);
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      const int64_t r0 = ch * rows_per;
+      const int64_t rows = std::min<int64_t>(rows_per, nq - r0);
+      if (rows <= 0) break;
+      const int64_t e0 = r0 * row_e, n = rows * row_e;
+      cudaEvent_t in_done = c.ev[2 * ch], att_done = c.ev[2 * ch + 1];
+      okp = cudaMemcpyAsync(dq + e0, q + e0, n * 4, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+            cudaEventRecord(in_done, st) == cudaSuccess &&
+            cudaStreamWaitEvent(c.comp, in_done, 0) == cudaSuccess;
+      if (!okp) return fail(CA_ERR_CUDA);
+      const int qblocks = static_cast<int>(std::min<long long>((n / 4 + 255) / 256 + 1, 148 * 8));
+      f32_to_bf16_kernel<<<qblocks, 256, 0, c.comp>>>(dq + e0, hq + e0, n);
+      if (cudaGetLastError() != cudaSuccess) return fail(CA_ERR_CUDA);
+      ca_dev_args d{};
+      d.q = hq + e0;
+      d.k = hk;
+      d.v = hv;
+      d.out = dout + e0;
+      d.out_f32 = 1;
+      d.precise = 1;
+      d.batch = 1;
+      d.sq = static_cast<int32_t>(rows);
+      d.sk = static_cast<int32_t>(nk);
+      d.n_head = static_cast<int32_t>(s->n_head);
+      d.n_head_kv = static_cast<int32_t>(s->n_head_kv);
+      d.head_dim = hd;
+      d.q_pos = dmeta + r0;
+      d.k_pos = dmeta + nq;
+      d.q_seq = qseq ? dmeta + off_qseq + r0 : (kseq ? dzero + r0 : nullptr);
+      d.k_seq = kseq ? dmeta + off_kseq : (qseq ? dzero : nullptr);
+      d.q_prefix = qpre ? dmeta + off_qpre + r0 : nullptr;
+      d.sliding_window = s->sliding_window;
+      d.causal_prefix = s->causal_prefix;
+      d.scale = s->scale;
+      d.softcap = s->softcap;
+      const int rc = attention_dev_impl(&d, c.comp);
+      if (rc != CA_OK) return fail(rc);
+      okp = cudaEventRecord(att_done, c.comp) == cudaSuccess &&
+            cudaStreamWaitEvent(c.outs, att_done, 0) == cudaSuccess &&
+            cudaMemcpyAsync(out + e0, dout + e0, n * 4, cudaMemcpyDeviceToHost, c.outs) ==
+                cudaSuccess;
+      if (!okp) return fail(CA_ERR_CUDA);
+    }
+    if (cudaStreamSynchronize(c.outs) != cudaSuccess ||
+        cudaStreamSynchronize(c.comp) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+      return fail(CA_ERR_CUDA);
+    int derr = 0;
+    if (cudaMemcpyFromSymbol(&derr, g_device_error, sizeof(int)) != cudaSuccess)
+      return fail(CA_ERR_CUDA);
+    if (derr != 0) {
+      const int zero = 0;
+      cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+      return CA_ERR_TIMEOUT;
+    }
+    return CA_OK;
+  }
   bool ok = cudaMemcpyAsync(dq, q, qe * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
   ok = ok && (ke == 0 || cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess);
   ok = ok && (ke == 0 || cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess);

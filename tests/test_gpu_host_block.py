@@ -83,6 +83,42 @@ def test_host_entry_block_diagonal_seq_ids_large():
     check_close(out, ref, H, hd, what="block-diagonal + prefix")
 
 
+@pytest.mark.parametrize("masks", ["none", "seq_prefix_window", "kseq_only"])
+def test_host_entry_pipelined_over_query_chunks(masks):
+    # Q of 4096 rows x 8 heads x 128 fp32 = 16 MiB: the host entry point runs
+    # its chunked copy-in / attention / copy-out pipeline (several launches
+    # over row ranges, metadata offset per chunk); results must match the
+    # one-shot semantics row for row.
+    rng = np.random.default_rng(5)
+    n, H, Hkv, hd = 4096, 8, 2, 128
+    lens = [2500, 1596]
+    pos = np.concatenate([np.arange(m) for m in lens])
+    seq = np.concatenate([np.full(m, i) for i, m in enumerate(lens)])
+    prefix = np.array([[300, 0][s_] for s_ in seq])
+    q = bf16_round(torch.from_numpy(rng.standard_normal(n * H * hd).astype(np.float32))).numpy()
+    k = bf16_round(torch.from_numpy(rng.standard_normal(n * Hkv * hd).astype(np.float32))).numpy()
+    v = bf16_round(torch.from_numpy(rng.standard_normal(n * Hkv * hd).astype(np.float32))).numpy()
+    kw = {}
+    if masks == "none":
+        qr, kr = ca.Rows(np.arange(n)), ca.Rows(np.arange(n))
+        shape = ca.AttnShape(n, n, H, Hkv, hd, scale=hd ** -0.5)
+    elif masks == "seq_prefix_window":
+        qr, kr = ca.Rows(pos, seq, prefix), ca.Rows(pos, seq)
+        shape = ca.AttnShape(n, n, H, Hkv, hd, sliding_window=700, scale=hd ** -0.5)
+        kw = dict(q_pos=pos, k_pos=pos, q_seq=seq, k_seq=seq, q_prefix=prefix,
+                  sliding_window=700)
+    else:  # key seq ids only: queries compare as sequence 0
+        qr, kr = ca.Rows(np.arange(n)), ca.Rows(np.arange(n), seq)
+        shape = ca.AttnShape(n, n, H, Hkv, hd, scale=hd ** -0.5)
+        kw = dict(k_seq=seq)
+    out = np.full(n * H * hd, np.inf, np.float32)
+    ca.attention(out, q, k, v, shape, qr, kr)
+    ref = orc.attention(q, k, v, nq=n, nk=n, n_head=H, n_head_kv=Hkv, head_dim=hd,
+                        scale=hd ** -0.5, kind=orc.ROW_AVX2 if orc.have_avx2()
+                        else orc.ROW_SCALAR, **kw)
+    check_close(out, ref, H, hd, what=f"pipelined host entry ({masks})")
+
+
 def _oracle_block(q, k, v, pos, wq, wk, rope, rope_dim, h, hkv, hd, eps):
     """Reference op order (forward.rs:296-310) on fp32 copies. The attention
     operands (post-RoPE Q/K) are then rounded to bf16, as the GPU's are: the
