@@ -272,7 +272,12 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
                    (!a->k_norm_w || aligned16(a->k_norm_w)) && a->rope_dim % 16 == 0;
   if (vec && (hd == 64 || hd == 128 || hd == 256)) {
     const long long toks = static_cast<long long>(a->batch) * a->n_active;
-    const long long pjobs = toks * ((H + 2 * Hkv + 15) / 16);
+    // 16-row jobs unless that leaves fewer jobs than 64 warps per SM; then
+    // one warp step per job (256 / head_dim rows).
+    pp.rows_per_job = 16;
+    if (toks * ((H + 2 * Hkv + 15) / 16) < 148LL * 64) pp.rows_per_job = 256 / hd;
+    const long long pjobs =
+        toks * ((H + 2 * Hkv + pp.rows_per_job - 1) / pp.rows_per_job);
     const int blocks = static_cast<int>(std::min<long long>((pjobs + 7) / 8, 148LL * 8));
     // head_dim 256 with full rotation: every NeoX pair inside one lane
     // (measured faster there; at 64 / 128 the partner-exchange form is).

@@ -30,6 +30,10 @@ struct PrepParams {
   __nv_bfloat16* cache_k;  // [batch, n_total, Hkv, hd]
   __nv_bfloat16* cache_v;
   int batch, na, n_total, H, Hkv, hd;
+  // Rows of one token per warp job in the vectorised kernels (a multiple of
+  // the rows a warp covers per step): 16 for large batches; small batches
+  // use one step per job so that more warps share the short pass.
+  int rows_per_job;
 };
 
 __device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
@@ -120,9 +124,8 @@ __global__ void __launch_bounds__(256) prep_token_kernel(const PrepParams p) {
   const int half = p.rope_dim / 2;
   const long long n_tok = static_cast<long long>(p.batch) * p.na;
   const int per_tok = p.H + 2 * p.Hkv;
-  // A job is up to kRowsPerJob rows of one token, so small batches still
-  // spread over many warps.
-  constexpr int kRowsPerJob = 16;
+  // A job is up to rows_per_job rows of one token.
+  const int kRowsPerJob = p.rows_per_job;
   const int chunks = (per_tok + kRowsPerJob - 1) / kRowsPerJob;
   const long long n_jobs = n_tok * chunks;
   float* buf = stage[warp][sub];
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(256) prep_pair_kernel(const PrepParams p) {
   constexpr int RPW = 32 / LPR;  // rows per warp per step
   constexpr int HD = LPR * 8;
   constexpr int HALF = HD / 2;
-  constexpr int kRowsPerJob = 16;
+  const int kRowsPerJob = p.rows_per_job;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPR, sl = lane % LPR;
   const int e0 = sl * 4;  // lower element block; the upper is e0 + HALF
