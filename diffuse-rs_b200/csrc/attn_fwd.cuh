@@ -320,7 +320,30 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
     const long long qpmin = qs[0], qpmax = qs[1];
     const int qsmin = qs[2], qsmax = qs[3], cmin = qs[4];
     const bool any_causal = qs[5] > 0, all_causal = qs[5] == nt;
-    for (int kt = w; kt < n_kt; kt += 2) {
+    // Keys with implicit positions (index = position) and no sequence ids:
+    // a tile's position range is arithmetic, so each thread classifies whole
+    // tiles with no loads or warp reductions (the sliding-window case).
+    const bool implicit_k = !p.k_pos && !p.k_seq;
+    for (int kt = implicit_k ? tid64 : n_kt; kt < n_kt; kt += 64) {
+      const int kpmin = kt * C::BN, kpmax = min(k_len, (kt + 1) * C::BN) - 1;
+      const bool ragged = (kt + 1) * C::BN > k_len;
+      uint16_t f = 2;
+      if (nt <= 0 || qsmax < 0 || 0 < qsmin) {
+        f = 0;
+      } else if (p.window != kNoWindow &&
+                 (kpmin - qpmax >= p.window || qpmin - kpmax >= p.window)) {
+        f = 0;
+      } else if (all_causal && kpmin > qpmax) {
+        f = 0;
+      } else if (qsmin == qsmax && qsmin == 0 &&
+                 (p.window == kNoWindow ||
+                  max(qpmax - kpmin, (long long)kpmax - qpmin) < p.window) &&
+                 (!any_causal || kpmax <= cmin)) {
+        f = ragged ? 3 : 1;
+      }
+      flags[kt] = f;
+    }
+    for (int kt = implicit_k ? n_kt : w; kt < n_kt; kt += 2) {
       int kpmin = INT_MAX, kpmax = INT_MIN, ksmin = INT_MAX, ksmax = INT_MIN;
 #pragma unroll
       for (int e = 0; e < C::BN / 32; ++e) {
