@@ -102,11 +102,12 @@ struct FwdParams {
 enum FwdMode { kSplit = 0, kAlt = 1 };
 
 
-template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_>
+template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_, int STK_ = ST_>
 struct FwdCfg {
   static constexpr int HDP = HDP_;  // head_dim padded to a multiple of 64
   static constexpr int BN = BN_;    // keys per tile
-  static constexpr int ST = ST_;    // stages of each of the K and V rings
+  static constexpr int ST = ST_;    // stages of the V ring
+  static constexpr int STK = STK_;  // stages of the K ring (Q K^T waits on K first)
   // PRECISE: P is split into bf16 hi + lo terms (two P V MMAs), so the
   // softmax weights reach the tensor core with ~16 significant bits, not 8.
   static constexpr bool PRECISE = PRECISE_;
@@ -124,15 +125,15 @@ struct FwdCfg {
   static constexpr int kKVBytes = kChunks * kKChunk;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;
-  static constexpr int kOffV = kOffK + ST * kKVBytes;
+  static constexpr int kOffV = kOffK + STK * kKVBytes;
   static constexpr int kOffBar = kOffV + ST * kKVBytes;
   // Barriers. K and V stages are released separately: a K stage as soon as
   // its Q K^T MMA completes, a V stage when its P V MMA(s) complete.
   static constexpr int kBarQ = 0;
-  static constexpr int kBarK = 1;             // [ST] K tile landed
-  static constexpr int kBarV = kBarK + ST;    // [ST] V tile landed
-  static constexpr int kBarKE = kBarV + ST;   // [ST] K stage free
-  static constexpr int kBarVE = kBarKE + ST;  // [ST] V stage free
+  static constexpr int kBarK = 1;             // [STK] K tile landed
+  static constexpr int kBarV = kBarK + STK;   // [ST] V tile landed
+  static constexpr int kBarKE = kBarV + ST;   // [STK] K stage free
+  static constexpr int kBarVE = kBarKE + STK; // [ST] V stage free
   static constexpr int kBarS = kBarVE + ST;   // [SB] S buffer holds Q K^T
   static constexpr int kBarP = kBarS + SB;    // [2] P written over S (per group)
   static constexpr int kBarO = kBarP + 2;     // [2] P V done (per O accumulator)
@@ -158,7 +159,7 @@ struct FwdCfg {
   static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 256, "tile shape");
   // The epilogue stages the output tile (up to fp32) in the idle K/V rings.
   static constexpr int kStageChunk = 128 * 128;  // one 128-byte column chunk, 128 rows
-  static_assert(128 * HDP * 4 <= 2 * ST * kKVBytes, "output staging fits in the K/V rings");
+  static_assert(128 * HDP * 4 <= (STK + ST) * kKVBytes, "output staging fits in the K/V rings");
 };
 
 // visible(): src/model/attention.rs:35-57 on int32 positions.
@@ -412,7 +413,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
-  constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST;
+  constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST, STK = C::STK;
   constexpr bool ALT = C::ALT, SPLIT = C::SPLIT;
   // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
   // static shared memory, so the dynamic window starts 1024-aligned; if it
@@ -445,10 +446,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (tid == 0) {
     mbar_init(bar(C::kBarQ), 1);
-    for (int s = 0; s < ST; ++s) {
+    for (int s = 0; s < STK; ++s) {
       mbar_init(bar(C::kBarK + s), 1);
-      mbar_init(bar(C::kBarV + s), 1);
       mbar_init(bar(C::kBarKE + s), 1);
+    }
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(bar(C::kBarV + s), 1);
       mbar_init(bar(C::kBarVE + s), 1);
     }
     for (int i = 0; i < C::SB; ++i) mbar_init(bar(C::kBarS + i), 1);
@@ -467,18 +470,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_load_3d(sQ + c * C::kQChunk, &tm_q, bar(C::kBarQ), c * 64, kvh * p.G, q_beg + t0);
     // Without masks the visible tiles are 0, 1, 2, ...: the first ring
     // stages of K and V load now too, overlapping the tile list and the
-    // TMEM allocation (the producers continue from stage ST).
+    // TMEM allocation (the producers continue from stage STK / ST).
     if (!p.any_mask) {
-      const int e = min(ST, (k_len + BN - 1) / BN);
-      for (int jj = 0; jj < e; ++jj) {
-        mbar_arrive_expect_tx(bar(C::kBarK + jj), C::kKVBytes);
-        mbar_arrive_expect_tx(bar(C::kBarV + jj), C::kKVBytes);
+      const int n_kt = (k_len + BN - 1) / BN;
+      const int ek = min(STK, n_kt), ev = min(ST, n_kt);
+      for (int jj = 0; jj < ek || jj < ev; ++jj) {
+        if (jj < ek) {
+          mbar_arrive_expect_tx(bar(C::kBarK + jj), C::kKVBytes);
 #pragma unroll
-        for (int c = 0; c < C::kChunks; ++c) {
-          tma_load_3d(sK + jj * C::kKVBytes + c * C::kKChunk, &tm_k, bar(C::kBarK + jj), c * 64,
-                      kvh, k_beg + jj * BN);
-          tma_load_3d(sV + jj * C::kKVBytes + c * C::kKChunk, &tm_v, bar(C::kBarV + jj), c * 64,
-                      kvh, k_beg + jj * BN);
+          for (int c = 0; c < C::kChunks; ++c)
+            tma_load_3d(sK + jj * C::kKVBytes + c * C::kKChunk, &tm_k, bar(C::kBarK + jj),
+                        c * 64, kvh, k_beg + jj * BN);
+        }
+        if (jj < ev) {
+          mbar_arrive_expect_tx(bar(C::kBarV + jj), C::kKVBytes);
+#pragma unroll
+          for (int c = 0; c < C::kChunks; ++c)
+            tma_load_3d(sV + jj * C::kKVBytes + c * C::kKChunk, &tm_v, bar(C::kBarV + jj),
+                        c * 64, kvh, k_beg + jj * BN);
         }
       }
     }
@@ -511,9 +520,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t ring = is_k ? sK : sV;
       const int full = is_k ? C::kBarK : C::kBarV;
       const int empty = is_k ? C::kBarKE : C::kBarVE;
-      for (int j = p.any_mask ? 0 : min(ST, n); j < n; ++j) {
-        const int s = j % ST;
-        if (j >= ST && !mbar_wait(bar(empty + s), ((j / ST) - 1) & 1, dead)) break;
+      const int NS = is_k ? STK : ST;  // stages of this ring
+      for (int j = p.any_mask ? 0 : min(NS, n); j < n; ++j) {
+        const int s = j % NS;
+        if (j >= NS && !mbar_wait(bar(empty + s), ((j / NS) - 1) & 1, dead)) break;
         const int krow = k_beg + (list[j] & 0x3fff) * BN;
         CA_EV(is_k ? 0 : 1, j);
         mbar_arrive_expect_tx(bar(full + s), C::kKVBytes);
@@ -525,7 +535,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // Leave no bulk copy in flight: wait (bounded) for the last loads.
       bool d2 = false;
       if (is_k) mbar_wait(bar(C::kBarQ), 0, d2);
-      for (int j = max(0, n - ST); j < n; ++j) mbar_wait(bar(full + j % ST), (j / ST) & 1, d2);
+      for (int j = max(0, n - NS); j < n; ++j) mbar_wait(bar(full + j % NS), (j / NS) & 1, d2);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -539,9 +549,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // kSplit issues S[j] after P V[j - 2], whose issue already waited for
       // P V[j - 3].
       auto issue_s = [&](int j) -> bool {
-        const int s = j % ST;
+        const int s = j % STK;
         const int sb = j % C::SB;
-        if (!mbar_wait(bar(C::kBarK + s), (j / ST) & 1, dead)) return false;
+        if (!mbar_wait(bar(C::kBarK + s), (j / STK) & 1, dead)) return false;
         CA_EV(13, j);
         if (ALT && j >= 2 && !mbar_wait(bar(C::kBarO + og(j - 2)), ouse(j - 2) & 1, dead))
           return false;
