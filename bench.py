@@ -195,7 +195,9 @@ class Workload:
                      k=[rnd(B, na, Hkv, hd) for _ in range(self.n_sets)],
                      v=[rnd(B, na, Hkv, hd) for _ in range(self.n_sets)],
                      cache_k=rnd(B, nt, Hkv, hd), cache_v=rnd(B, nt, Hkv, hd),
-                     q_work=torch.empty(B, na, H, hd, dtype=bf, device=device),
+                     # Rotated Q for the attention-only timing; the fused
+                     # block (head_dim 128, small grids) leaves it unwritten.
+                     q_work=rnd(B, na, H, hd),
                      out=torch.empty(B, na, H, hd, dtype=bf, device=device))
             if cfg["qk_norm"]:
                 L["wq"] = torch.rand(hd, generator=g, device=device) + 0.5

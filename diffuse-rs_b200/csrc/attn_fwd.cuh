@@ -90,6 +90,14 @@ struct FwdParams {
   float scale_log2;   // scale * log2(e)
   float softcap;      // 0 = off
   int tma_out;        // uniform batch: the epilogue stores O through tm_o
+  // Fused Q pre-ops (head_dim 128, rotation over the full head): the Q tile
+  // is loaded pre-norm, pre-RoPE and the softmax warps apply the per-head
+  // RMSNorm (gains fq_w, may be null) and NeoX RoPE (table fq_rope, entry
+  // (pos, i) at 2 (pos * 64 + i)) in shared memory before the first Q K^T.
+  int fuse_q;
+  const float* fq_w;
+  const float* fq_rope;
+  float fq_eps;
   int any_mask;       // any of: seq ids, prefixes, window, causal prefix (positions
                       // alone mask nothing: they matter only to those masks)
 };
@@ -139,7 +147,8 @@ struct FwdCfg {
   static constexpr int kBarO = kBarP + 2;     // [2] P V done (per O accumulator)
   static constexpr int kBarF = kBarO + 2;     // all MMAs done
   static constexpr int kBarX = kBarF + 1;     // [4] softmax warp-pair exchange
-  static constexpr int kNumBars = kBarX + 4;
+  static constexpr int kBarQR = kBarX + 4;    // fused Q pre-ops done
+  static constexpr int kNumBars = kBarQR + 1;
   // Largest key-tile count per sequence (keys <= kMaxTiles * BN).
   static constexpr int kMaxTiles = 1024;
   static constexpr int kOffList = kOffBar + kNumBars * 8;
@@ -407,6 +416,90 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
 
 namespace ca {
 
+// Fused Q pre-ops, run by the 256 softmax threads once the raw Q tile has
+// landed: thread tt owns row tt / 2 and the NeoX pairs (i, i + 64) for i in
+// 32 (tt & 1) .. +31, i.e. 16-byte units of both 64-column chunks of the
+// 128-byte-swizzled tile (unit u of row r sits at u ^ (r & 7)). Arithmetic is
+// that of the pre-ops kernel (norm_heads / rms_norm_inplace, src/model/ops.rs:
+// 107-114, 385-389; rotate_rows :432-452): f32 squares summed in f64 (exact
+// for bf16 inputs), scale = 1 / (float)sqrt(ss / 128 + eps), x * scale * w,
+// then (a, b) -> (a cos - b sin, a sin + b cos), rounded to bf16 in place.
+// The writes are fenced for the tensor core's (async) proxy, the 256 threads
+// meet at a named barrier and one arrival releases the first Q K^T.
+template <class C>
+__device__ __forceinline__ void fuse_q_prep(const FwdParams& p, uint32_t sQ, uint32_t bar_q,
+                                            uint32_t bar_qr, int t0, int q_beg, int q_len,
+                                            int tt, bool& dead) {
+  mbar_wait(bar_q, 0, dead);
+  const int r = tt >> 1, h = tt & 1;
+  const int t_local = t0 + r / p.G;
+  const bool valid = !dead && r < p.R && t_local < q_len;
+  // Four 16-byte units per chunk: units 4h .. 4h + 3 (columns 32h .. 32h + 31).
+  uint32_t lo[16], hi[16];
+  const uint32_t row_lo = sQ + r * 128, row_hi = sQ + C::kQChunk + r * 128;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) lo[i] = hi[i] = 0u;
+  if (valid) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t off = static_cast<uint32_t>(((4 * h + u) ^ (r & 7)) << 4);
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(lo[4 * u]), "=r"(lo[4 * u + 1]), "=r"(lo[4 * u + 2]), "=r"(lo[4 * u + 3])
+                   : "r"(row_lo + off));
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(hi[4 * u]), "=r"(hi[4 * u + 1]), "=r"(hi[4 * u + 2]), "=r"(hi[4 * u + 3])
+                   : "r"(row_hi + off));
+    }
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float a0 = __uint_as_float(lo[i] << 16), a1 = __uint_as_float(lo[i] & 0xffff0000u);
+    const float b0 = __uint_as_float(hi[i] << 16), b1 = __uint_as_float(hi[i] & 0xffff0000u);
+    ss += static_cast<double>(__fmul_rn(a0, a0));
+    ss += static_cast<double>(__fmul_rn(a1, a1));
+    ss += static_cast<double>(__fmul_rn(b0, b0));
+    ss += static_cast<double>(__fmul_rn(b1, b1));
+  }
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);  // the row's other half (adjacent lane)
+  if (valid) {
+    const int pos = p.q_pos ? p.q_pos[q_beg + t_local] : t_local;
+    const bool norm = p.fq_w != nullptr;
+    const float sc =
+        __fdiv_rn(1.f, static_cast<float>(sqrt(ss / 128.0 + static_cast<double>(p.fq_eps))));
+    const float* cs_row = p.fq_rope + 2 * (static_cast<long long>(pos) * 64 + 32 * h);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float a[2] = {__uint_as_float(lo[i] << 16), __uint_as_float(lo[i] & 0xffff0000u)};
+      float b[2] = {__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xffff0000u)};
+      const float4 t = __ldg(reinterpret_cast<const float4*>(cs_row) + i);  // (sin, cos) x 2
+      const float sn[2] = {t.x, t.z}, cs[2] = {t.y, t.w};
+      float ya[2], yb[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = 32 * h + 2 * i + e;
+        if (norm) {
+          a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(p.fq_w + col));
+          b[e] = __fmul_rn(__fmul_rn(b[e], sc), __ldg(p.fq_w + 64 + col));
+        }
+        ya[e] = __fsub_rn(__fmul_rn(a[e], cs[e]), __fmul_rn(b[e], sn[e]));
+        yb[e] = __fadd_rn(__fmul_rn(a[e], sn[e]), __fmul_rn(b[e], cs[e]));
+      }
+      lo[i] = pack_bf16(ya[0], ya[1]);
+      hi[i] = pack_bf16(yb[0], yb[1]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t off = static_cast<uint32_t>(((4 * h + u) ^ (r & 7)) << 4);
+      st_shared_v4(row_lo + off, lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
+      st_shared_v4(row_hi + off, hi[4 * u], hi[4 * u + 1], hi[4 * u + 2], hi[4 * u + 3]);
+    }
+  }
+  fence_proxy_async_smem();
+  named_bar_sync(3, 256);
+  if (tt == 0) mbar_arrive(bar_qr);
+}
+
 template <class C>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -461,6 +554,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     mbar_init(bar(C::kBarF), 1);
     for (int i = 0; i < 4; ++i) mbar_init(bar(C::kBarX + i), 2);
+    mbar_init(bar(C::kBarQR), 1);
     fence_barrier_init();
     fence_proxy_async_smem();
     // Q does not depend on the tile list: start its load right away.
@@ -604,7 +698,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // the other group's softmax covers the gap. kSplit: S[j+2] takes the
       // buffer of P[j-1], so the tensor core runs P V[j] and S[j+2] back to
       // back while the softmax works on S[j+1].
-      if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead)) {
+      if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead) &&
+          (!p.fuse_q || mbar_wait(bar(C::kBarQR), 0, dead))) {
         bool ok = issue_s(0) && (n < 2 || issue_s(1));
         for (int j = 0; ok && j < n; ++j) ok = issue_pv(j) && (j + 2 >= n || issue_s(j + 2));
       }
@@ -648,6 +743,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const float cap_l2 = p.softcap * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
     int used = 0;  // tiles this thread has processed
+
+    if constexpr (HDP == 128) {
+      if (p.fuse_q) fuse_q_prep<C>(p, sQ, bar(C::kBarQ), bar(C::kBarQR), t0, q_beg, q_len,
+                                   (warp - 3) * 32 + lane, dead);
+    }
 
     for (int j = ALT ? grp : 0; j < n; j += ALT ? 2 : 1) {
       const int entry = list[j];

@@ -141,7 +141,17 @@ int clamp_opt(int64_t v) {  // Option<usize> as int32 (None = -1)
 }  // namespace
 
 // Validates a device-args struct and launches the attention kernel.
-int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
+// Fused Q pre-ops for the block path (see FwdParams::fuse_q).
+#ifndef CA_FUSE_Q
+#define CA_FUSE_Q 1
+#endif
+struct QFuse {
+  const float* w;     // q norm gains [128] or null
+  const float* rope;  // [rope_len, 64, 2] (sin, cos)
+  float eps;
+};
+
+int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = nullptr) {
   if (!a || !a->q || !a->k || !a->v || !a->out) return CA_ERR_INVALID;
   const int H = a->n_head, Hkv = a->n_head_kv, hd = a->head_dim;
   if (H <= 0 || Hkv <= 0 || hd <= 0 || a->batch < 0) return CA_ERR_INVALID;
@@ -208,6 +218,11 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st) {
                    ? 1
                    : 0;
 
+  p.fuse_q = fq != nullptr;
+  p.fq_w = fq ? fq->w : nullptr;
+  p.fq_rope = fq ? fq->rope : nullptr;
+  p.fq_eps = fq ? fq->eps : 0.f;
+
   Launch L{a, &p, total_q, total_k, max_sq, max_sk, qrs, krs, st};
   // One Q tile per CTA. head_dim <= 192: the two softmax groups alternate
   // key tiles (kAlt). head_dim 256: they split every tile's key columns
@@ -262,22 +277,34 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   pp.batch = a->batch;
   pp.na = a->n_active;
   pp.n_total = a->n_total;
-  pp.H = H;
-  pp.Hkv = Hkv;
-  pp.hd = hd;
-  const long long jobs = static_cast<long long>(a->batch) * a->n_active * (H + 2 * Hkv);
   const bool vec = aligned16(a->q) && aligned16(a->k) && aligned16(a->v) &&
                    aligned16(a->q_work) && aligned16(a->cache_k) && aligned16(a->cache_v) &&
                    aligned16(a->rope) && (!a->q_norm_w || aligned16(a->q_norm_w)) &&
                    (!a->k_norm_w || aligned16(a->k_norm_w)) && a->rope_dim % 16 == 0;
+  // head_dim 128 with rotation over the whole head: the attention kernel
+  // normalises and rotates its own Q tile (each Q row belongs to exactly one
+  // CTA), so the pre-ops pass covers K and V only and Q never round-trips
+  // through HBM; q_work is then unused.
+  // The in-kernel pass lengthens every CTA's prologue, paid once per wave of
+  // CTAs: measured on B200 it wins up to a few waves (c2 7 waves -5%, c4 and
+  // c1 one wave -7% / even) and loses at c3's 28 waves (+3%).
+  const long long fq_ctas = static_cast<long long>(a->batch) * Hkv *
+                            ((a->n_active + 128 / (H / Hkv) - 1) / (128 / (H / Hkv)));
+  const bool fuse_q = CA_FUSE_Q && vec && hd == 128 && a->rope_dim == 128 &&
+                      H / Hkv <= 128 && fq_ctas <= 148LL * 8;
+  const int Hp = fuse_q ? 0 : H;  // Q rows handled by the pre-ops pass
+  pp.H = Hp;
+  pp.Hkv = Hkv;
+  pp.hd = hd;
+  const long long jobs = static_cast<long long>(a->batch) * a->n_active * (Hp + 2 * Hkv);
   if (vec && (hd == 64 || hd == 128 || hd == 256)) {
     const long long toks = static_cast<long long>(a->batch) * a->n_active;
     // 16-row jobs unless that leaves fewer jobs than 64 warps per SM; then
     // one warp step per job (256 / head_dim rows).
     pp.rows_per_job = 16;
-    if (toks * ((H + 2 * Hkv + 15) / 16) < 148LL * 64) pp.rows_per_job = 256 / hd;
+    if (toks * ((Hp + 2 * Hkv + 15) / 16) < 148LL * 64) pp.rows_per_job = 256 / hd;
     const long long pjobs =
-        toks * ((H + 2 * Hkv + pp.rows_per_job - 1) / pp.rows_per_job);
+        toks * ((Hp + 2 * Hkv + pp.rows_per_job - 1) / pp.rows_per_job);
     const int blocks = static_cast<int>(std::min<long long>((pjobs + 7) / 8, 148LL * 8));
     // head_dim 256 with full rotation: every NeoX pair inside one lane
     // (measured faster there; at 64 / 128 the partner-exchange form is).
@@ -292,7 +319,7 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   if (cudaGetLastError() != cudaSuccess) return CA_ERR_CUDA;
 
   ca_dev_args d{};
-  d.q = a->q_work;
+  d.q = fuse_q ? a->q : a->q_work;
   d.k = a->cache_k;
   d.v = a->cache_v;
   d.out = a->out;
@@ -309,6 +336,10 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   d.scale = a->scale;
   d.softcap = a->softcap;
   d.precise = a->precise;
+  if (fuse_q) {
+    const QFuse fq{a->q_norm_w, a->rope, a->rms_eps};
+    return attention_dev_impl(&d, st, &fq);
+  }
   return attention_dev_impl(&d, st);
 }
 
