@@ -145,7 +145,9 @@ typedef struct {
     void* cache_k;             /* bf16 [batch, n_total, n_head_kv, head_dim] */
     void* cache_v;
     int32_t n_total;           /* positions per sequence; keys = all n_total positions */
-    void* q_work;              /* bf16 [batch, n_active, n_head, head_dim] scratch (caller-owned) */
+    void* q_work;              /* bf16 [batch, n_active, n_head, head_dim] scratch (caller-owned);
+                                  its contents are unspecified after the call (small head_dim-128
+                                  calls rotate Q inside the attention kernel and leave it unwritten) */
     void* out;                 /* [batch, n_active, n_head, head_dim] */
     int32_t out_f32;
     int32_t n_head;
