@@ -286,12 +286,13 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   // CTA), so the pre-ops pass covers K and V only and Q never round-trips
   // through HBM; q_work is then unused.
   // The in-kernel pass lengthens every CTA's prologue, paid once per wave of
-  // CTAs: measured on B200 it wins up to a few waves (c2 7 waves -5%, c4 and
-  // c1 one wave -7% / even) and loses at c3's 28 waves (+3%).
+  // CTAs and not amortised over few key tiles: measured on B200 (bench.py
+  // steps, same box) c2 (7 waves, 8 key tiles) -2.7%, c4 (1 wave, 33 tiles)
+  // -1%, c1 (1 key tile) +7%, c3 (28 waves) +3%.
   const long long fq_ctas = static_cast<long long>(a->batch) * Hkv *
                             ((a->n_active + 128 / (H / Hkv) - 1) / (128 / (H / Hkv)));
   const bool fuse_q = CA_FUSE_Q && vec && hd == 128 && a->rope_dim == 128 &&
-                      H / Hkv <= 128 && fq_ctas <= 148LL * 8;
+                      H / Hkv <= 128 && fq_ctas <= 148LL * 8 && a->n_total >= 512;
   const int Hp = fuse_q ? 0 : H;  // Q rows handled by the pre-ops pass
   pp.H = Hp;
   pp.Hkv = Hkv;

@@ -131,13 +131,15 @@ def _oracle_block(q, k, v, pos, wq, wk, rope, rope_dim, h, hkv, hd, eps):
     return rb(q), rb(k), v
 
 
-@pytest.mark.parametrize("qk_norm,hd,rope_dim,hkv", [
-    (False, 128, 128, 4), (True, 128, 128, 4),
-    (True, 64, 64, 2), (True, 256, 256, 2),       # 256: lane-paired pre-ops
-    (True, 128, 64, 4),                           # partial rotation
+@pytest.mark.parametrize("qk_norm,hd,rope_dim,hkv,S", [
+    (False, 128, 128, 4, 600), (True, 128, 128, 4, 600),  # Q pre-ops inside the attention
+    (True, 128, 128, 2, 600),
+    (True, 128, 128, 4, 300),                     # < 512 keys: separate pre-ops pass
+    (True, 64, 64, 2, 300), (True, 256, 256, 2, 300),  # 256: lane-paired pre-ops
+    (True, 128, 64, 4, 300),                      # partial rotation
 ])
-def test_block_without_cache(qk_norm, hd, rope_dim, hkv):
-    B, S, H, Hkv = 2, 300, 4, hkv
+def test_block_without_cache(qk_norm, hd, rope_dim, hkv, S):
+    B, H, Hkv = 2, 4, hkv
     eps, theta = 1e-6, 50000.0
     g = torch.Generator().manual_seed(31)
     q = bf16_round(randn(g, B, S, H, hd))
