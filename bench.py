@@ -173,32 +173,41 @@ class ClockSampler:
 
 
 class Workload:
-    """Device tensors for one rank's batch of one config."""
+    """Device tensors for one rank's batch of one config.
 
-    def __init__(self, cfg, device, seed):
+    heads=(q0, q1, kv0, kv1) keeps only that head range of a global batch
+    generated from the same seed on every rank (the head-sharded form)."""
+
+    def __init__(self, cfg, device, seed, heads=None):
         import torch
         import canvas_attn as ca
         self.ca, self.torch, self.cfg = ca, torch, cfg
         B, na, nt, H, Hkv, hd = (cfg[k] for k in ("B", "na", "n_total", "H", "Hkv", "hd"))
         g = torch.Generator(device=device).manual_seed(seed)
         bf = torch.bfloat16
+        q0, q1, kv0, kv1 = heads if heads is not None else (0, H, 0, Hkv)
+        self.H, self.Hkv = q1 - q0, kv1 - kv0
 
-        def rnd(*shape):
-            return torch.randn(*shape, generator=g, device=device, dtype=torch.float32).to(bf)
+        def rnd(*shape, sl=None):
+            t = torch.randn(*shape, generator=g, device=device, dtype=torch.float32).to(bf)
+            if sl is None or (sl[0] == 0 and sl[1] == shape[2]):
+                return t
+            return t[:, :, sl[0]:sl[1]].contiguous()
 
+        qs, kvs = (q0, q1), (kv0, kv1)
         self.n_sets = 2  # fresh active Q/K/V alternate between steps
         self.layers = []
         for (window, theta) in cfg["layers"]:
             rope = torch.from_numpy(ca.build_rope_cache(max(4096, nt), hd, theta)).to(device)
             L = dict(window=window, rope=rope, rope_len=max(4096, nt),
-                     q=[rnd(B, na, H, hd) for _ in range(self.n_sets)],
-                     k=[rnd(B, na, Hkv, hd) for _ in range(self.n_sets)],
-                     v=[rnd(B, na, Hkv, hd) for _ in range(self.n_sets)],
-                     cache_k=rnd(B, nt, Hkv, hd), cache_v=rnd(B, nt, Hkv, hd),
+                     q=[rnd(B, na, H, hd, sl=qs) for _ in range(self.n_sets)],
+                     k=[rnd(B, na, Hkv, hd, sl=kvs) for _ in range(self.n_sets)],
+                     v=[rnd(B, na, Hkv, hd, sl=kvs) for _ in range(self.n_sets)],
+                     cache_k=rnd(B, nt, Hkv, hd, sl=kvs), cache_v=rnd(B, nt, Hkv, hd, sl=kvs),
                      # Rotated Q for the attention-only timing; the fused
                      # block (head_dim 128, small grids) leaves it unwritten.
-                     q_work=rnd(B, na, H, hd),
-                     out=torch.empty(B, na, H, hd, dtype=bf, device=device))
+                     q_work=rnd(B, na, H, hd, sl=qs),
+                     out=torch.empty(B, na, self.H, hd, dtype=bf, device=device))
             if cfg["qk_norm"]:
                 L["wq"] = torch.rand(hd, generator=g, device=device) + 0.5
                 L["wk"] = torch.rand(hd, generator=g, device=device) + 0.5
@@ -207,24 +216,31 @@ class Workload:
         self.pos = pos.repeat(B, 1).contiguous()
         self.stream = torch.cuda.current_stream(device)
 
-    def block_args(self, L, i):
+    def block_args(self, L, i, b0=0, b1=None):
+        """Block arguments for sequences b0..b1-1 of input set i."""
         c = self.cfg
+        b1 = c["B"] if b1 is None else b1
+        sl = slice(b0, b1)
         return self.ca.make_block_args(
-            L["q"][i], L["k"][i], L["v"][i], batch=c["B"], n_active=c["na"],
-            active_pos=self.pos, rope=L["rope"], rope_len=L["rope_len"], rope_dim=c["hd"],
-            cache_k=L["cache_k"], cache_v=L["cache_v"], n_total=c["n_total"],
-            q_work=L["q_work"], out=L["out"], n_head=c["H"], n_head_kv=c["Hkv"],
-            head_dim=c["hd"], q_norm_w=L.get("wq"), k_norm_w=L.get("wk"), rms_eps=1e-6,
-            sliding_window=L["window"], scale=c["scale"], softcap=c["softcap"])
+            L["q"][i][sl], L["k"][i][sl], L["v"][i][sl], batch=b1 - b0, n_active=c["na"],
+            active_pos=self.pos[sl], rope=L["rope"], rope_len=L["rope_len"],
+            rope_dim=c["hd"], cache_k=L["cache_k"][sl], cache_v=L["cache_v"][sl],
+            n_total=c["n_total"], q_work=L["q_work"][sl], out=L["out"][sl], n_head=self.H,
+            n_head_kv=self.Hkv, head_dim=c["hd"], q_norm_w=L.get("wq"),
+            k_norm_w=L.get("wk"), rms_eps=1e-6, sliding_window=L["window"],
+            scale=c["scale"], softcap=c["softcap"])
+
+    def block(self, L, i, b0=0, b1=None, stream=None):
+        import ctypes
+        a = self.block_args(L, i % self.n_sets, b0, b1)
+        sp = (stream or self.stream).cuda_stream
+        rc = self.ca.lib.ca_attention_block_dev(ctypes.byref(a), sp)
+        if rc != 0:
+            raise self.ca.CaError(rc, "ca_attention_block_dev")
 
     def step(self, i):
-        import ctypes
-        sp = self.stream.cuda_stream
         for L in self.layers:
-            a = self.block_args(L, i % self.n_sets)
-            rc = self.ca.lib.ca_attention_block_dev(ctypes.byref(a), sp)
-            if rc != 0:
-                raise self.ca.CaError(rc, "ca_attention_block_dev")
+            self.block(L, i)
 
     launches_per_step = property(lambda self: 2 * len(self.layers))
 
@@ -232,7 +248,7 @@ class Workload:
         c = self.cfg
         return self.ca.make_dev_args(
             L["q_work"], L["cache_k"], L["cache_v"], L["out"], batch=c["B"], sq=c["na"],
-            sk=c["n_total"], n_head=c["H"], n_head_kv=c["Hkv"], head_dim=c["hd"],
+            sk=c["n_total"], n_head=self.H, n_head_kv=self.Hkv, head_dim=c["hd"],
             q_pos=self.pos, sliding_window=L["window"], scale=c["scale"],
             softcap=c["softcap"])
 
@@ -323,6 +339,23 @@ class CpuSample:
         return (f"{rows} (head, query) rows of the {config} config (one sequence, repeated "
                 f"when the sample exceeds it) over {len(self.cfg['layers'])} layer(s), "
                 f"{self.cfg['n_total']} keys each")
+
+
+def cpu_baseline(cfg, config, seconds, repeats=3):
+    """The oracle's AVX2 row kernel on all host threads: one fixed row sample
+    (sized for about seconds / repeats), run `repeats` times; the median rate
+    with the spread of the repeats."""
+    cs = CpuSample(cfg)
+    n_rows = cs.calibrate(seconds / repeats)
+    rates, secs, rows = [], 0.0, 0
+    for _ in range(repeats):
+        f, s, rows = cs.run(n_rows)
+        rates.append(f / s / 1e12)
+        secs += s
+    return dict(value=statistics.median(rates), unit="TFLOP/s", cores=cs.threads, kind="port",
+                spread=[round(min(rates), 5), round(max(rates), 5)], repeats=repeats,
+                sample=cs.describe(rows, config) + f", median of {repeats} repeats, "
+                f"{secs:.1f} s in all")
 
 
 class E2E:
@@ -427,42 +460,155 @@ def physical_gpu_index(local):
     return local
 
 
-def run_head_sharded(args, cfg, world, dev):
+def input_bytes_of(cfg):
+    """Bytes of one step's inputs on one rank (Q/K/V of every layer plus the
+    K/V cache), bf16; equals Workload.input_bytes()."""
+    B, na, nt, H, Hkv, hd = (cfg[k] for k in ("B", "na", "n_total", "H", "Hkv", "hd"))
+    return len(cfg["layers"]) * 2 * B * hd * (na * H + 2 * na * Hkv + 2 * nt * Hkv)
+
+
+def config_dict(args, cfg, world):
+    """The workload description both arms print (same keys and values)."""
+    flush = input_bytes_of(cfg) < 2 * L2_BYTES
+    return {"workload": args.config, "desc": cfg["desc"], "batch_per_gpu": cfg["B"],
+            "global_batch": cfg["B"] * world, "seq_q": cfg["na"], "seq_k": cfg["n_total"],
+            "layers": len(cfg["layers"]),
+            "l2": "flushed between steps (working set < 2x L2)" if flush
+            else "inputs larger than L2, no flush",
+            "parallelism": f"dp{world} (independent sequences per rank)"}
+
+
+def kernel_ms(wl, flush, scratch, reps):
+    """Average device time (CUDA events on the launching stream) of the
+    attention kernel alone, per layer, on the workload's prepared tensors."""
     import torch
-    from canvas_attn.sharding import gather_heads
-    local = dict(cfg, H=cfg["H"] // world, Hkv=cfg["Hkv"] // world)
-    wl = Workload(local, dev, seed=4321 + int(os.environ.get("RANK", "0")))
-    tok = cfg["B"] * cfg["na"]
+    out = []
+    for L in wl.layers:
+        wl.attn_only(L)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(reps)]
+        torch.cuda.synchronize()
+        for a, b in ev:
+            if flush:
+                scratch.zero_()
+            a.record(wl.stream)
+            wl.attn_only(L)
+            b.record(wl.stream)
+        torch.cuda.synchronize()
+        out.append(sum(a.elapsed_time(b) for a, b in ev) / reps)
+    return out
 
-    def gather_all():
-        return [gather_heads(L["out"].view(tok, local["H"], cfg["hd"])) for L in wl.layers]
 
-    for i in range(args.warmup):
-        wl.step(i)
-        gather_all()
-    torch.cuda.synchronize()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    barrier(world)
-    torch.cuda.synchronize()
-    for i in range(args.steps):
-        ev[i][0].record(wl.stream)
-        wl.step(i)
-        ev[i][1].record(wl.stream)
-        full = gather_all()
-        ev[i][2].record(wl.stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    assert full[0].shape == (tok, cfg["H"], cfg["hd"])
-    comp = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in ev), world)
-    tot = max_over_ranks(sum(a.elapsed_time(c) for a, _, c in ev), world)
+def roofline(name, cfg, layers, ms, peaks, traffic_key=None):
+    """Roofline of the attention kernel over `layers` of a config taking `ms`:
+    c4 against HBM copy bandwidth (algorithmic bytes), the others against the
+    burst bf16 tensor peak (algorithmic flops)."""
+    if name == "c4":
+        achieved = len(layers) * layer_bytes(cfg) / (ms * 1e-3) / 1e9
+        r = dict(bound="hbm", achieved=round(achieved, 1), peak=peaks["hbm"], unit="GB/s",
+                 peak_source=peaks["source"] + " copy")
+    else:
+        fl = sum(layer_flops(cfg, w) for w, _ in layers)
+        r = dict(bound="tensor", achieved=round(fl / (ms * 1e-3) / 1e12, 1),
+                 peak=peaks["tflops"], unit="TFLOP/s", peak_source=peaks["source"] + " burst")
+    r["frac"] = round(r["achieved"] / r["peak"], 4)
+    r["traffic"] = load_traffic(traffic_key or name)
+    r["kernel_ms"] = round(ms, 4)
+    return r
+
+
+def run_head_sharded(args, cfg, world, rank, dev):
+    """Head-sharded strong scaling of ONE global batch of the config: rank r
+    computes kv heads [r * Hkv / N, (r + 1) * Hkv / N) and their query heads
+    of every sequence; per layer the batch runs in chunks of sequences, and
+    while chunk c+1 computes, chunk c's head slices are all-gathered (NCCL, on
+    a second stream) and placed into [tokens, n_head, head_dim] rows, the
+    layout o_proj consumes (src/model/forward.rs:345). Every rank generates
+    the same global inputs from one seed; rank 0 then recomputes the whole
+    batch on its own GPU and compares the gathered rows with it."""
+    import torch
+    import torch.distributed as dist
+    from canvas_attn.sharding import head_shard
+    sh = head_shard(cfg["H"], cfg["Hkv"], world, rank)
+    wl = Workload(cfg, dev, seed=4321, heads=(sh.q_begin, sh.q_end, sh.kv_begin, sh.kv_end))
+    B, na, H, hd = cfg["B"], cfg["na"], cfg["H"], cfg["hd"]
+    lh = wl.H
+    n_chunks = max(1, min(args.hs_chunks, B))
+    while B % n_chunks:
+        n_chunks -= 1
+    bc = B // n_chunks
+    tok_c = bc * na
+    comm = torch.cuda.Stream(dev)
+    stage = torch.empty((n_chunks, world, tok_c, lh, hd), dtype=torch.bfloat16, device=dev)
+    full = [torch.empty((B * na, H, hd), dtype=torch.bfloat16, device=dev) for _ in wl.layers]
+    done = [torch.cuda.Event() for _ in range(n_chunks)]
+
+    def step(i, gather=True):
+        for li, L in enumerate(wl.layers):
+            for c in range(n_chunks):
+                wl.block(L, i, c * bc, (c + 1) * bc)
+                if not gather:
+                    continue
+                done[c].record(wl.stream)
+                comm.wait_event(done[c])
+                with torch.cuda.stream(comm):
+                    src = L["out"][c * bc:(c + 1) * bc].view(-1)
+                    dist.all_gather_into_tensor(stage[c].view(-1), src)
+                    # [world, tok_c, lh, hd] -> rows tok of [tokens, H, hd]
+                    full[li][c * tok_c:(c + 1) * tok_c].view(tok_c, world, lh, hd).copy_(
+                        stage[c].permute(1, 0, 2, 3))
+        if gather:
+            fin = torch.cuda.Event()
+            fin.record(comm)
+            wl.stream.wait_event(fin)
+
+    def timed(gather):
+        for i in range(args.warmup):
+            step(i, gather)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        barrier(world)
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            ev[i][0].record(wl.stream)
+            step(i, gather)
+            ev[i][1].record(wl.stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(sum(a.elapsed_time(b) for a, b in ev), world)
+
+    comp = timed(False)
+    tot = timed(True)
+    last = (args.steps - 1) % wl.n_sets
+    # Parity: rank 0 recomputes the whole global batch (all heads) on its own
+    # GPU from the same inputs and compares with the gathered rows.
+    parity = None
+    if rank == 0:
+        ref = Workload(cfg, dev, seed=4321)
+        for L in ref.layers:
+            ref.block(L, last)
+        torch.cuda.synchronize()
+        worst, exact = 0.0, True
+        for li, L in enumerate(ref.layers):
+            want = L["out"].view(B * na, H, hd)
+            exact = exact and torch.equal(full[li], want)
+            worst = max(worst, (full[li].float() - want.float()).abs().max().item())
+        parity = dict(max_abs_diff=worst, bit_identical=exact, rows_checked=B * na * H,
+                      against="all heads of the same global batch run on one GPU")
+        del ref
+        torch.cuda.synchronize()
     flops = step_flops(cfg) * args.steps
     return dict(value=round(flops / (tot * 1e-3) / 1e12, 2), unit="TFLOP/s",
                 compute_only=round(flops / (comp * 1e-3) / 1e12, 2),
                 ms_per_step=round(tot / args.steps, 4),
-                gather_ms_per_step=round((tot - comp) / args.steps, 4),
-                heads_per_rank=local["H"], kv_heads_per_rank=local["Hkv"],
-                global_batch=cfg["B"], scaling="strong",
-                collective="one NCCL all_gather_into_tensor per layer")
+                compute_ms_per_step=round(comp / args.steps, 4),
+                heads_per_rank=lh, kv_heads_per_rank=wl.Hkv,
+                global_batch=B, scaling="strong", chunks=n_chunks,
+                collective=("per layer and chunk of sequences, one NCCL "
+                            "all_gather_into_tensor on a second stream, overlapped "
+                            "with the next chunk's compute"),
+                parity=parity)
 
 
 def run_ours(args, cfg):
@@ -472,6 +618,7 @@ def run_ours(args, cfg):
     dev = torch.device("cuda", local)
     wl = Workload(cfg, dev, seed=1234 + rank)
     ws = wl.input_bytes()
+    assert ws == input_bytes_of(cfg)
     flush = ws < 2 * L2_BYTES
     scratch = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
 
@@ -503,35 +650,38 @@ def run_ours(args, cfg):
     value = world * flops * args.steps / (ms_total * 1e-3) / 1e12
 
     # Dominant kernel: the attention kernel alone, on the same prepared tensors.
-    reps = max(3, min(args.steps, 50))
-    attn_ms = 0.0
-    for L in wl.layers:
-        wl.attn_only(L)
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(reps)]
-        torch.cuda.synchronize()
-        for a, b in ev:
-            if flush:
-                scratch.zero_()
-            a.record(wl.stream)
-            wl.attn_only(L)
-            b.record(wl.stream)
-        torch.cuda.synchronize()
-        attn_ms += sum(a.elapsed_time(b) for a, b in ev) / reps
     peaks = load_peaks()
-    hbm_bound = args.config == "c4"
-    if hbm_bound:
-        per_launch = sum(layer_bytes(cfg) for _ in cfg["layers"])
-        achieved = per_launch / (attn_ms * 1e-3) / 1e9
-        roof = dict(bound="hbm", achieved=round(achieved, 1), peak=peaks["hbm"], unit="GB/s")
-    else:
-        achieved = flops / (attn_ms * 1e-3) / 1e12
-        roof = dict(bound="tensor", achieved=round(achieved, 1), peak=peaks["tflops"],
-                    unit="TFLOP/s")
-    roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
-    roof["peak_source"] = peaks["source"] + (" burst" if not hbm_bound else " copy")
-    roof["traffic"] = load_traffic(args.config)
-    roof["kernel_ms"] = round(attn_ms, 4)
+    reps = max(3, min(args.steps, 50))
+    attn_ms = sum(kernel_ms(wl, flush, scratch, reps))
+    roof = roofline(args.config, cfg, cfg["layers"], attn_ms, peaks)
+
+    # The attention kernel alone on the other tensor/HBM-bound configs, so
+    # that one run records every config's roofline (1 GPU only).
+    by_config = None
+    if world == 1 and not args.no_by_config:
+        by_config = {}
+        for name in ("c2", "c4", "c5"):
+            if name == args.config:
+                continue
+            c = CONFIGS[name]
+            w2 = Workload(c, dev, seed=99)
+            fl2 = w2.input_bytes() < 2 * L2_BYTES
+            for i in range(3):
+                w2.step(i)  # writes q_work (the rotated Q the kernel-alone run reads)
+            ms = kernel_ms(w2, fl2, scratch if fl2 else None, reps)
+            if name == "c5":  # sliding-window layers and the global layer apart
+                slide = [k for k, (w, _) in enumerate(c["layers"]) if w is not None]
+                glob = [k for k, (w, _) in enumerate(c["layers"]) if w is None]
+                by_config["c5_sliding"] = roofline(
+                    name, c, [c["layers"][slide[0]]], statistics.mean(ms[k] for k in slide),
+                    peaks, "c5_sliding")
+                by_config["c5_global"] = roofline(name, c, [c["layers"][glob[0]]],
+                                                  ms[glob[0]], peaks, "c5_global")
+            else:
+                by_config[name] = roofline(name, c, c["layers"], sum(ms), peaks)
+            del w2
+            torch.cuda.synchronize()
+        torch.cuda.empty_cache()
 
     # Head sharding (N > 1): every rank computes its kv-head slice (and the
     # query heads of those groups) of ONE global batch of the config, then
@@ -540,7 +690,7 @@ def run_ours(args, cfg):
     # compute-only and with the gather, both max over ranks.
     head_sharded = None
     if world > 1 and cfg["Hkv"] % world == 0 and not args.no_head_shard:
-        head_sharded = run_head_sharded(args, cfg, world, dev)
+        head_sharded = run_head_sharded(args, cfg, world, rank, dev)
 
     # End to end through the host-buffer drop-in entry point.
     e2e = None
@@ -560,11 +710,7 @@ def run_ours(args, cfg):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cs = CpuSample(cfg)
-        n_rows = cs.calibrate(args.cpu_seconds)
-        f, s, rows = cs.run(n_rows)
-        cpu = dict(value=f / s / 1e12, unit="TFLOP/s", cores=cs.threads, kind="port",
-                   sample=cs.describe(rows, args.config) + f", {s:.1f} s")
+        cpu = cpu_baseline(cfg, args.config, args.cpu_seconds)
 
     if rank == 0:
         line = {
@@ -580,16 +726,10 @@ def run_ours(args, cfg):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1), bf16)",
-            "config": {"workload": args.config, "desc": cfg["desc"],
-                       "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * world,
-                       "seq_q": cfg["na"], "seq_k": cfg["n_total"],
-                       "layers": len(cfg["layers"]),
-                       "tokens_per_s": round(world * cfg["B"] * cfg["na"] * args.steps
-                                             / (ms_total * 1e-3), 1),
-                       "l2": "flushed between steps (working set < 2x L2)" if flush
-                       else "inputs larger than L2, no flush",
-                       "parallelism": f"dp{world} (independent sequences per rank)"},
+            "config": config_dict(args, cfg, world),
+            "tokens_per_s": round(world * cfg["B"] * cfg["na"] * args.steps / (ms_total * 1e-3), 1),
             "roofline": roof,
+            "roofline_by_config": by_config,
             "head_sharded": head_sharded,
             "cpu_baseline": cpu,
             "e2e": e2e,
@@ -610,15 +750,19 @@ def run_reference(args, cfg):
     if rank != 0:
         return
     cs = CpuSample(cfg)
-    n_rows = cs.calibrate(args.ref_step_seconds)
+    # Each step is the same bounded row sample, sized so that the whole run
+    # stays within about two minutes of CPU time.
+    n_rows = cs.calibrate(min(args.ref_step_seconds, 120.0 / max(1, args.steps)))
     for _ in range(args.warmup):
         cs.run(max(16, n_rows // 8))
     tf, ts, tr = 0.0, 0.0, 0
+    rates = []
     for _ in range(args.steps):
         f, s, rows = cs.run(n_rows)
         tf += f
         ts += s
         tr += rows
+        rates.append(f / s / 1e12)
     value = tf / ts / 1e12
     sample = cs.describe(tr // max(1, args.steps), args.config) + " per step"
     line = {
@@ -635,9 +779,10 @@ def run_reference(args, cfg):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": args.config, "desc": cfg["desc"]},
+        "config": config_dict(args, cfg, world),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cs.threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "spread": [round(min(rates), 5), round(max(rates), 5)],
+                         "median": round(statistics.median(rates), 5)},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -658,6 +803,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-head-shard", action="store_true",
                     help="skip the head-sharded (all-gather) leg under torchrun")
+    ap.add_argument("--no-by-config", action="store_true",
+                    help="skip the kernel-alone rooflines of the other configs")
+    ap.add_argument("--hs-chunks", type=int, default=4,
+                    help="chunks of sequences the head-sharded leg pipelines")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "ca_build_rope_table",
     "ca_device_status",
     "ca_selftest_wait_timeout",
+    "ca_selftest_wait_timeout_status",
     "ca_status_string",
     "ca_version",
 )
@@ -79,7 +80,7 @@ class CaDevArgs(ctypes.Structure):
                 ("k_seq", ctypes.c_void_p), ("q_prefix", ctypes.c_void_p),
                 ("sliding_window", ctypes.c_int64), ("causal_prefix", ctypes.c_int64),
                 ("scale", ctypes.c_float), ("softcap", ctypes.c_float),
-                ("precise", ctypes.c_int32)]
+                ("precise", ctypes.c_int32), ("status", ctypes.c_void_p)]
 
 
 class CaBlockArgs(ctypes.Structure):
@@ -95,7 +96,8 @@ class CaBlockArgs(ctypes.Structure):
                 ("n_head", ctypes.c_int32), ("n_head_kv", ctypes.c_int32),
                 ("head_dim", ctypes.c_int32), ("sliding_window", ctypes.c_int64),
                 ("causal_prefix", ctypes.c_int64), ("scale", ctypes.c_float),
-                ("softcap", ctypes.c_float), ("precise", ctypes.c_int32)]
+                ("softcap", ctypes.c_float), ("precise", ctypes.c_int32),
+                ("status", ctypes.c_void_p)]
 
 
 def _load():
@@ -120,6 +122,9 @@ def _load():
     L.ca_device_status.restype = ctypes.c_int
     L.ca_selftest_wait_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p]
     L.ca_selftest_wait_timeout.restype = ctypes.c_int
+    L.ca_selftest_wait_timeout_status.argtypes = [ctypes.c_int64, ctypes.c_void_p,
+                                                  ctypes.c_void_p]
+    L.ca_selftest_wait_timeout_status.restype = ctypes.c_int
     L.ca_status_string.argtypes = [ctypes.c_int]
     L.ca_status_string.restype = ctypes.c_char_p
     L.ca_version.restype = ctypes.c_char_p
@@ -232,7 +237,7 @@ def make_dev_args(q, k, v, out, *, batch, sq, sk, n_head, n_head_kv, head_dim,
                   q_pos=None, k_pos=None, q_seq=None, k_seq=None, q_prefix=None,
                   sliding_window=None, causal_prefix=None, scale=1.0, softcap=0.0,
                   q_row_stride=0, kv_row_stride=0, out_row_stride=0,
-                  precise=False) -> CaDevArgs:
+                  precise=False, status=None) -> CaDevArgs:
     return CaDevArgs(_ptr(q), _ptr(k), _ptr(v), _ptr(out), 1 if out_f32 else 0,
                      q_row_stride, kv_row_stride, out_row_stride, batch, sq, sk,
                      _ptr(cu_q), _ptr(cu_k), max_sq, total_q, total_k,
@@ -240,7 +245,7 @@ def make_dev_args(q, k, v, out, *, batch, sq, sk, n_head, n_head_kv, head_dim,
                      _ptr(k_seq), _ptr(q_prefix),
                      -1 if sliding_window is None else int(sliding_window),
                      -1 if causal_prefix is None else int(causal_prefix),
-                     float(scale), float(softcap), 1 if precise else 0)
+                     float(scale), float(softcap), 1 if precise else 0, _ptr(status))
 
 
 def attention_dev(q, k, v, out, *, stream=None, **kw) -> None:
@@ -257,14 +262,14 @@ def make_block_args(q, k, v, *, batch, n_active, active_pos, rope, rope_len, rop
                     cache_k, cache_v, n_total, q_work, out, n_head, n_head_kv, head_dim,
                     q_norm_w=None, k_norm_w=None, v_norm=False, rms_eps=1e-6,
                     out_f32=False, sliding_window=None, causal_prefix=None, scale=1.0,
-                    softcap=0.0, precise=False) -> CaBlockArgs:
+                    softcap=0.0, precise=False, status=None) -> CaBlockArgs:
     return CaBlockArgs(_ptr(q), _ptr(k), _ptr(v), batch, n_active, _ptr(active_pos),
                        _ptr(q_norm_w), _ptr(k_norm_w), 1 if v_norm else 0, float(rms_eps),
                        _ptr(rope), rope_len, rope_dim, _ptr(cache_k), _ptr(cache_v), n_total,
                        _ptr(q_work), _ptr(out), 1 if out_f32 else 0, n_head, n_head_kv,
                        head_dim, -1 if sliding_window is None else int(sliding_window),
                        -1 if causal_prefix is None else int(causal_prefix), float(scale),
-                       float(softcap), 1 if precise else 0)
+                       float(softcap), 1 if precise else 0, _ptr(status))
 
 
 def attention_block_dev(*args, stream=None, **kw) -> None:
@@ -300,7 +305,8 @@ def build_rope_cache(max_seq_len: int, rope_dim: int, theta: float,
 
 
 def device_status(stream=None) -> int:
-    """Synchronises `stream`, then reads and clears the device error word."""
+    """Synchronises `stream`, then reads and clears the device-wide error word
+    (the word of launches that were given no status word of their own)."""
     return int(lib.ca_device_status(_stream(stream)))
 
 
@@ -310,3 +316,11 @@ def selftest_wait_timeout(limit_ns: int, stream=None) -> None:
     expiry shows up in the next device_status() as CA_ERR_TIMEOUT."""
     _check(lib.ca_selftest_wait_timeout(int(limit_ns), _stream(stream)),
            "ca_selftest_wait_timeout")
+
+
+def selftest_wait_timeout_status(limit_ns: int, status, stream=None) -> None:
+    """The same self-test, reporting to the caller's device int32 `status`
+    (a per-call status word as in make_dev_args(status=...)) instead of the
+    device-wide word."""
+    _check(lib.ca_selftest_wait_timeout_status(int(limit_ns), _ptr(status), _stream(stream)),
+           "ca_selftest_wait_timeout_status")

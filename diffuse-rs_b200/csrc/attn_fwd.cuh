@@ -39,34 +39,6 @@ namespace ca {
 
 constexpr int kNoWindow = INT_MAX;
 
-// Pipeline event timestamps of one CTA, compiled in only with -DCA_TRACE
-// (a diagnostic build; the product library never records them).
-#ifdef CA_TRACE
-#ifndef CA_TRACE_X
-#define CA_TRACE_X 5
-#endif
-__device__ long long g_trace[16][64];
-#define CA_EV(kind, j)                                                              \
-  do {                                                                              \
-    if (blockIdx.x == CA_TRACE_X && blockIdx.y == 3 && blockIdx.z == 1 && (j) < 64)          \
-      g_trace[kind][j] = clock64();                                                 \
-  } while (0)
-// Per softmax warp (8 warps x 4 events x 64 tiles).
-__device__ long long g_trace_w[8][4][64];
-#define CA_EVW(e, j)                                                                    \
-  do {                                                                                  \
-    if (lane == 0 && blockIdx.x == CA_TRACE_X && blockIdx.y == 3 && blockIdx.z == 1 &&  \
-        (j) < 64)                                                                       \
-      g_trace_w[warp - 3][e][j] = clock64();                                            \
-  } while (0)
-#else
-#define CA_EVW(e, j) \
-  do {               \
-  } while (0)
-#define CA_EV(kind, j) \
-  do {                 \
-  } while (0)
-#endif
 constexpr int kFwdThreads = 352;  // 3 control warps + 8 softmax warps
 
 struct FwdParams {
@@ -100,6 +72,7 @@ struct FwdParams {
   float fq_eps;
   int any_mask;       // any of: seq ids, prefixes, window, causal prefix (positions
                       // alone mask nothing: they matter only to those masks)
+  int* err;           // device status word of this launch (null: g_device_error)
 };
 
 // Softmax organisation of a CTA (see the file comment):
@@ -289,7 +262,6 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
   const int lane = tid64 & 31;
   const int w = tid64 >> 5;  // 0..1
   const int n_kt = (k_len + C::BN - 1) / C::BN;
-  if (tid64 == 0) CA_EV(15, 4);
   if (!p.any_mask) {
     for (int kt = tid64; kt < n_kt; kt += 64)
       flags[kt] = ((kt + 1) * C::BN <= k_len) ? 1 : 3;
@@ -390,9 +362,7 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
       }
     }
   }
-  if (tid64 == 0) CA_EV(15, 5);
   named_bar_sync(1, 64);
-  if (tid64 == 0) CA_EV(15, 6);
   if (w == 0) {
     int count = 0;
     for (int base = 0; base < n_kt; base += 32) {
@@ -408,7 +378,6 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
       count += __popc(ball);
     }
     if (lane == 0) misc[1] = count;
-    if (lane == 0) CA_EV(15, 7);
   }
 }
 
@@ -430,7 +399,7 @@ template <class C>
 __device__ __forceinline__ void fuse_q_prep(const FwdParams& p, uint32_t sQ, uint32_t bar_q,
                                             uint32_t bar_qr, int t0, int q_beg, int q_len,
                                             int tt, bool& dead) {
-  mbar_wait(bar_q, 0, dead);
+  mbar_wait(bar_q, 0, dead, p.err);
   const int r = tt >> 1, h = tt & 1;
   const int t_local = t0 + r / p.G;
   const bool valid = !dead && r < p.R && t_local < q_len;
@@ -513,7 +482,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   // ever did not, report it instead of computing garbage.
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_u32(smem) & 1023u) != 0) {
-    if (threadIdx.x == 0) atomicExch(&g_device_error, kErrLayout);
+    if (threadIdx.x == 0) atomicExch(p.err ? p.err : &g_device_error, kErrLayout);
     return;
   }
   const int tid = threadIdx.x;
@@ -527,7 +496,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   seq_range(p, b, q_beg, q_len, k_beg, k_len);
   const int t0 = qtile * p.QT;  // first query token of this CTA
   if (t0 >= q_len) return;           // uniform across the CTA
-  if (threadIdx.x == 0) CA_EV(14, 0);
 
   const uint32_t sQ = smem_u32(smem + C::kOffQ);
   const uint32_t sK = smem_u32(smem + C::kOffK);
@@ -585,20 +553,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
     }
-    CA_EV(15, 0);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(misc), C::kTmemCols);
     tmem_relinquish();
-    if (lane == 0) CA_EV(15, 1);
   }
   if (warp <= 1)
     build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, t0, p.QT, list, misc, tid);
-  if (tid == 32) CA_EV(15, 2);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (tid == 0) CA_EV(15, 3);
   const uint32_t tmem = static_cast<uint32_t>(misc[0]);
   const int n = misc[1];
   bool dead = false;
@@ -617,9 +581,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int NS = is_k ? STK : ST;  // stages of this ring
       for (int j = p.any_mask ? 0 : min(NS, n); j < n; ++j) {
         const int s = j % NS;
-        if (j >= NS && !mbar_wait(bar(empty + s), ((j / NS) - 1) & 1, dead)) break;
+        if (j >= NS && !mbar_wait(bar(empty + s), ((j / NS) - 1) & 1, dead, p.err)) break;
         const int krow = k_beg + (list[j] & 0x3fff) * BN;
-        CA_EV(is_k ? 0 : 1, j);
         mbar_arrive_expect_tx(bar(full + s), C::kKVBytes);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
@@ -628,8 +591,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       // Leave no bulk copy in flight: wait (bounded) for the last loads.
       bool d2 = false;
-      if (is_k) mbar_wait(bar(C::kBarQ), 0, d2);
-      for (int j = max(0, n - NS); j < n; ++j) mbar_wait(bar(full + j % NS), (j / NS) & 1, d2);
+      if (is_k) mbar_wait(bar(C::kBarQ), 0, d2, p.err);
+      for (int j = max(0, n - NS); j < n; ++j) mbar_wait(bar(full + j % NS), (j / NS) & 1, d2, p.err);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -645,11 +608,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       auto issue_s = [&](int j) -> bool {
         const int s = j % STK;
         const int sb = j % C::SB;
-        if (!mbar_wait(bar(C::kBarK + s), (j / STK) & 1, dead)) return false;
-        CA_EV(13, j);
-        if (ALT && j >= 2 && !mbar_wait(bar(C::kBarO + og(j - 2)), ouse(j - 2) & 1, dead))
+        if (!mbar_wait(bar(C::kBarK + s), (j / STK) & 1, dead, p.err)) return false;
+        if (ALT && j >= 2 && !mbar_wait(bar(C::kBarO + og(j - 2)), ouse(j - 2) & 1, dead, p.err))
           return false;
-        CA_EV(2, j);
         tc_fence_after();
         const uint32_t kbase = sK + s * C::kKVBytes;
 #pragma unroll
@@ -659,7 +620,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           umma_ss(tmem + sb * BN, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar(C::kBarS + sb));
-        CA_EV(10, j);
         umma_commit(bar(C::kBarKE + s));
         return true;
       };
@@ -668,13 +628,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       auto issue_pv = [&](int i) -> bool {
         const int s = i % ST;
         const int g = og(i), use = ouse(i);
-        if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead)) return false;
-        CA_EV(12, i);
-        if (!mbar_wait(bar(C::kBarP + g), use & 1, dead)) return false;
+        if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead, p.err)) return false;
+        if (!mbar_wait(bar(C::kBarP + g), use & 1, dead, p.err)) return false;
         // kSplit: P V[i - 1] done (frees the buffer S[i + 2] takes). Checked
         // before P V[i] is issued, so the O barrier is at most one phase on.
-        if (SPLIT && i > 0 && !mbar_wait(bar(C::kBarO), (i - 1) & 1, dead)) return false;
-        CA_EV(3, i);
+        if (SPLIT && i > 0 && !mbar_wait(bar(C::kBarO), (i - 1) & 1, dead, p.err)) return false;
         tc_fence_after();
         const uint32_t vbase = sV + s * C::kKVBytes;
         const uint32_t pcol = tmem + (i % C::SB) * BN;
@@ -689,7 +647,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
         }
         umma_commit(bar(C::kBarO + g));
-        CA_EV(11, i);
         umma_commit(bar(C::kBarVE + s));
         return true;
       };
@@ -698,15 +655,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // the other group's softmax covers the gap. kSplit: S[j+2] takes the
       // buffer of P[j-1], so the tensor core runs P V[j] and S[j+2] back to
       // back while the softmax works on S[j+1].
-      if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead) &&
-          (!p.fuse_q || mbar_wait(bar(C::kBarQR), 0, dead))) {
+      if (n > 0 && mbar_wait(bar(C::kBarQ), 0, dead, p.err) &&
+          (!p.fuse_q || mbar_wait(bar(C::kBarQR), 0, dead, p.err))) {
         bool ok = issue_s(0) && (n < 2 || issue_s(1));
         for (int j = 0; ok && j < n; ++j) ok = issue_pv(j) && (j + 2 >= n || issue_s(j + 2));
       }
       // Every MMA this thread issued completes before the role ends.
       umma_commit(bar(C::kBarF));
       bool d2 = false;
-      mbar_wait(bar(C::kBarF), 0, d2);
+      mbar_wait(bar(C::kBarF), 0, d2, p.err);
     }
   } else {
     // ------------------------------------------------------------ softmax
@@ -754,11 +711,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int kt = entry & 0x3fff;
       const int kind = entry >> 14;  // 0 full, 1 ragged end, 2 masked
       const int sb = j % C::SB;
-      mbar_wait(bar(C::kBarS + sb), (j / C::SB) & 1, dead);
+      mbar_wait(bar(C::kBarS + sb), (j / C::SB) & 1, dead, p.err);
       dead = __any_sync(0xffffffffu, dead);
       if (dead) break;
-      if ((warp & 3) == 2 && lane == 0) CA_EV(5, j);
-      CA_EVW(0, j);
       tc_fence_after();
       // Each thread reads its row of S from TMEM once (32-column loads, one
       // wait) and keeps it in registers: pass 1 forms the row max, pass 2
@@ -891,15 +846,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         rmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       }
-      if ((warp & 3) == 2 && lane == 0) CA_EV(6, j);
-      CA_EVW(1, j);
       if constexpr (SPLIT) {
         // Combine with the partner warp (same rows, other key columns).
         float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
         xch[((j & 1) * 2 + grp) * 128 + r] = rmax;
         __syncwarp();
         if (lane == 0) mbar_arrive(xbar);
-        mbar_wait(xbar, j & 1, dead);
+        mbar_wait(xbar, j & 1, dead, p.err);
         dead = __any_sync(0xffffffffu, dead);
         if (dead) break;
         rmax = fmaxf(rmax, xch[((j & 1) * 2 + (grp ^ 1)) * 128 + r]);
@@ -924,7 +877,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
 
-      if ((warp & 3) == 2 && lane == 0) CA_EV(7, j);
       // Pass 2: exponentiate and write P into the S buffer, in the layout the
       // P V MMA reads as its TMEM A operand: the 16 keys of block kk take
       // columns 16 kk .. 16 kk + 15, bf16 pairs of the hi terms in the first 8
@@ -1031,15 +983,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       sum4[3] += sum2[1].y;
 #endif
       l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-      if ((warp & 3) == 2 && lane == 0) CA_EV(8, j);
-      CA_EVW(2, j);
       // kAlt: this group's previous P V completed before S[j] was computed.
       // kSplit: the previous P V (tile j - 1) may still run; wait for it. The
       // wait also keeps the O barrier from running two phases ahead of any
       // waiter (P V[j] cannot start before this warp's P arrival below).
       if constexpr (SPLIT) {
         if (used > 0) {
-          mbar_wait(bar(C::kBarO), (j - 1) & 1, dead);
+          mbar_wait(bar(C::kBarO), (j - 1) & 1, dead, p.err);
           dead = __any_sync(0xffffffffu, dead);
           if (dead) break;
           tc_fence_after();
@@ -1062,28 +1012,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if ((warp & 3) == 2 && lane == 0) CA_EV(9, j);
-      CA_EVW(3, j);
       if (lane == 0) mbar_arrive(bar(C::kBarP + pg));
       ++used;
     }
 
     // ------------------------------------------------------------ epilogue
-    if ((warp & 3) == 2 && lane == 0) CA_EV(14, 2 + grp);
     // Wait for this group's last P V. kAlt: merge the two groups' (max, sum, O) partials. kSplit: add the two
     // halves' row sums (same running max).
     // kAlt: wait until every MMA is done (the output is staged in the K/V
     // rings; this also covers a group that had no tile of its own).
     if (ALT && n > 0 && !dead) {
-      mbar_wait(bar(C::kBarF), 0, dead);
+      mbar_wait(bar(C::kBarF), 0, dead, p.err);
       dead = __any_sync(0xffffffffu, dead);
       tc_fence_after();
     } else if (used > 0 && !dead) {
-      mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead);
+      mbar_wait(bar(C::kBarO + pg), (used - 1) & 1, dead, p.err);
       dead = __any_sync(0xffffffffu, dead);
       tc_fence_after();
     }
-    if ((warp & 3) == 2 && lane == 0) CA_EV(14, 4 + grp);
     bool have = n > 0 && !dead;
     float s_me = 1.f, s_ot = 0.f, inv = __int_as_float(0x7fc00000);
     const int n_me = ALT ? (grp == 0 ? (n + 1) / 2 : n / 2) : n;
@@ -1097,12 +1043,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (ALT) xo[128 + r] = m;
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
-      mbar_wait(xbar, ALT ? 0 : (n & 1), dead);
+      mbar_wait(xbar, ALT ? 0 : (n & 1), dead, p.err);
       dead = __any_sync(0xffffffffu, dead);
       have = !dead;
       tc_fence_after();
       const float l_ot = xp[r];
-      if ((warp & 3) == 2 && lane == 0) CA_EV(14, 6 + grp);
       if (ALT) {
         const float m_ot = xp[128 + r];
         const float mt = fmaxf(n_me > 0 ? m : -INFINITY, n_ot > 0 ? m_ot : -INFINITY);
@@ -1215,12 +1160,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         bulk_wait_group_read0();
       }
     }
-    if ((warp & 3) == 2 && lane == 0) CA_EV(14, 8 + grp);
   }
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) CA_EV(14, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);

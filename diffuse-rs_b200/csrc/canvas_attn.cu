@@ -218,6 +218,7 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
                    ? 1
                    : 0;
 
+  p.err = a->status;
   p.fuse_q = fq != nullptr;
   p.fq_w = fq ? fq->w : nullptr;
   p.fq_rope = fq ? fq->rope : nullptr;
@@ -248,6 +249,26 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
 namespace ca {
 namespace {
 
+// Whether the block path rotates Q inside the attention kernel (head_dim 128
+// with rotation over the whole head, grids of at most 8 waves, at least 512
+// keys); q_work is then neither written nor read. `vec`: every pointer is
+// 16-byte aligned and rope_dim % 16 == 0.
+bool block_fuses_q(const ca_block_args* a, bool vec) {
+  const int H = a->n_head, Hkv = a->n_head_kv;
+  if (!CA_FUSE_Q || !vec || a->head_dim != 128 || a->rope_dim != 128 || H / Hkv > 128)
+    return false;
+  const long long fq_ctas = static_cast<long long>(a->batch) * Hkv *
+                            ((a->n_active + 128 / (H / Hkv) - 1) / (128 / (H / Hkv)));
+  return fq_ctas <= 148LL * 8 && a->n_total >= 512;
+}
+
+bool block_vec(const ca_block_args* a) {
+  return aligned16(a->q) && aligned16(a->k) && aligned16(a->v) && aligned16(a->q_work) &&
+         aligned16(a->cache_k) && aligned16(a->cache_v) && aligned16(a->rope) &&
+         (!a->q_norm_w || aligned16(a->q_norm_w)) && (!a->k_norm_w || aligned16(a->k_norm_w)) &&
+         a->rope_dim % 16 == 0;
+}
+
 int block_impl(const ca_block_args* a, cudaStream_t st) {
   if (!a || !a->q || !a->k || !a->v || !a->active_pos || !a->rope || !a->cache_k ||
       !a->cache_v || !a->q_work || !a->out)
@@ -277,10 +298,7 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   pp.batch = a->batch;
   pp.na = a->n_active;
   pp.n_total = a->n_total;
-  const bool vec = aligned16(a->q) && aligned16(a->k) && aligned16(a->v) &&
-                   aligned16(a->q_work) && aligned16(a->cache_k) && aligned16(a->cache_v) &&
-                   aligned16(a->rope) && (!a->q_norm_w || aligned16(a->q_norm_w)) &&
-                   (!a->k_norm_w || aligned16(a->k_norm_w)) && a->rope_dim % 16 == 0;
+  const bool vec = block_vec(a);
   // head_dim 128 with rotation over the whole head: the attention kernel
   // normalises and rotates its own Q tile (each Q row belongs to exactly one
   // CTA), so the pre-ops pass covers K and V only and Q never round-trips
@@ -289,10 +307,7 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   // CTAs and not amortised over few key tiles: measured on B200 (bench.py
   // steps, same box) c2 (7 waves, 8 key tiles) -2.7%, c4 (1 wave, 33 tiles)
   // -1%, c1 (1 key tile) +7%, c3 (28 waves) +3%.
-  const long long fq_ctas = static_cast<long long>(a->batch) * Hkv *
-                            ((a->n_active + 128 / (H / Hkv) - 1) / (128 / (H / Hkv)));
-  const bool fuse_q = CA_FUSE_Q && vec && hd == 128 && a->rope_dim == 128 &&
-                      H / Hkv <= 128 && fq_ctas <= 148LL * 8 && a->n_total >= 512;
+  const bool fuse_q = block_fuses_q(a, vec);
   const int Hp = fuse_q ? 0 : H;  // Q rows handled by the pre-ops pass
   pp.H = Hp;
   pp.Hkv = Hkv;
@@ -337,6 +352,7 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   d.scale = a->scale;
   d.softcap = a->softcap;
   d.precise = a->precise;
+  d.status = a->status;
   if (fuse_q) {
     const QFuse fq{a->q_norm_w, a->rope, a->rms_eps};
     return attention_dev_impl(&d, st, &fq);
@@ -416,7 +432,8 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
   const size_t b_qf = align_up(qe * 4), b_kf = align_up(ke * 4);
   const size_t b_qh = align_up(qe_p * 2), b_kh = align_up(ke_p * 2);
   const size_t b_out = hd_p == hd ? 0 : align_up(qe_p * 4);
-  const size_t b_meta = align_up(meta.size() * 4 + 4 * (nq + nk));
+  // Metadata, the zero ids of a one-sided seq test, and this call's status word.
+  const size_t b_meta = align_up(meta.size() * 4 + 4 * (nq + nk) + 4);
   // Layout: [q f32 | k f32 | v f32 | q bf16 | k bf16 | v bf16 | out f32 | meta].
   // With no padding the fp32 output overwrites the fp32 Q staging copy.
   const size_t need = b_qf + 2 * b_kf + b_qh + 2 * b_kh + b_out + b_meta;
@@ -439,6 +456,14 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
   float* dout = b_out ? reinterpret_cast<float*>(carve(b_out)) : dq;
   int32_t* dmeta = reinterpret_cast<int32_t*>(carve(b_meta));
   int32_t* dzero = dmeta + meta.size();
+  int32_t* dstatus = dzero + nq + nk;
+  // Reads this call's status word after the stream work is done.
+  auto call_status = [&]() -> int {
+    int32_t derr = 0;
+    if (cudaMemcpy(&derr, dstatus, sizeof(derr), cudaMemcpyDeviceToHost) != cudaSuccess)
+      return CA_ERR_CUDA;
+    return derr == 0 ? CA_OK : CA_ERR_TIMEOUT;
+  };
   cudaStream_t st = c.stream;
   // Large calls without head_dim padding run as a pipeline over chunks of
   // query rows on three streams: K, V and the row metadata are copied in
@@ -473,6 +498,7 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
                cudaMemcpyAsync(dmeta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice,
                                st) == cudaSuccess;
     if (okp && qseq != kseq) okp = cudaMemsetAsync(dzero, 0, 4 * (nq + nk), st) == cudaSuccess;
+    okp = okp && cudaMemsetAsync(dstatus, 0, 4, st) == cudaSuccess;
     okp = okp && cudaEventRecord(c.ev[2 * kMaxChunks], st) == cudaSuccess &&
           cudaStreamWaitEvent(c.comp, c.ev[2 * kMaxChunks], 0) == cudaSuccess;
     if (!okp) return fail(CA_ERR_CUDA);
@@ -514,6 +540,7 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
       d.causal_prefix = s->causal_prefix;
       d.scale = s->scale;
       d.softcap = s->softcap;
+      d.status = dstatus;
       const int rc = attention_dev_impl(&d, c.comp);
       if (rc != CA_OK) return fail(rc);
       okp = cudaEventRecord(att_done, c.comp) == cudaSuccess &&
@@ -525,15 +552,7 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
     if (cudaStreamSynchronize(c.outs) != cudaSuccess ||
         cudaStreamSynchronize(c.comp) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
       return fail(CA_ERR_CUDA);
-    int derr = 0;
-    if (cudaMemcpyFromSymbol(&derr, g_device_error, sizeof(int)) != cudaSuccess)
-      return fail(CA_ERR_CUDA);
-    if (derr != 0) {
-      const int zero = 0;
-      cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
-      return CA_ERR_TIMEOUT;
-    }
-    return CA_OK;
+    return call_status();
   }
   bool ok = cudaMemcpyAsync(dq, q, qe * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
   ok = ok && (ke == 0 || cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess);
@@ -542,6 +561,7 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
                  cudaSuccess;
   if ((qseq != kseq) && ok)
     ok = cudaMemsetAsync(dzero, 0, 4 * (nq + nk), st) == cudaSuccess;
+  ok = ok && cudaMemsetAsync(dstatus, 0, 4, st) == cudaSuccess;
   if (!ok) return CA_ERR_CUDA;
   auto conv = [&](const float* src, __nv_bfloat16* dst, long long n, long long n_p) {
     const int blocks = static_cast<int>(std::min<long long>((n_p / 4 + 255) / 256 + 1, 148 * 8));
@@ -578,6 +598,7 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
   d.causal_prefix = s->causal_prefix;
   d.scale = s->scale;
   d.softcap = s->softcap;
+  d.status = dstatus;
   int rc = nk == 0 ? CA_OK : attention_dev_impl(&d, st);
   if (rc != CA_OK) return rc;
   if (nk == 0) {  // no key at all: every row is 0 * (1 / 0)
@@ -593,14 +614,7 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
     return CA_ERR_CUDA;
   }
   if (cudaStreamSynchronize(st) != cudaSuccess) return CA_ERR_CUDA;
-  int derr = 0;
-  if (cudaMemcpyFromSymbol(&derr, g_device_error, sizeof(int)) != cudaSuccess) return CA_ERR_CUDA;
-  if (derr != 0) {
-    const int zero = 0;
-    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
-    return CA_ERR_TIMEOUT;
-  }
-  return CA_OK;
+  return call_status();
 }
 
 }  // namespace
@@ -615,34 +629,55 @@ namespace {
 constexpr size_t kNoAllocElems = CA_NOALLOC_SCRATCH_BYTES / sizeof(__nv_bfloat16);
 static __device__ __align__(256) __nv_bfloat16 g_noalloc_qwork[kNoAllocElems];
 
+// Per-device address of g_noalloc_qwork. Only a successful lookup is
+// cached: a failed one (for example a first call made while the stream is
+// being captured) is retried by the next call.
 struct NoAllocSlot {
-  std::once_flag once;
+  std::mutex mu;
   void* ptr = nullptr;
-  int rc = CA_ERR_CUDA;
 };
 NoAllocSlot g_noalloc[kMaxDevices];
+
+int noalloc_scratch(int dev, void** out) {
+  NoAllocSlot& slot = g_noalloc[dev];
+  std::lock_guard<std::mutex> lock(slot.mu);
+  if (!slot.ptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_qwork) != cudaSuccess || !ptr) {
+      cudaGetLastError();  // clear the error so that it does not surface in a later call
+      return CA_ERR_CUDA;
+    }
+    slot.ptr = ptr;
+  }
+  *out = slot.ptr;
+  return CA_OK;
+}
 
 int noalloc_impl(const ca_block_args* a, cudaStream_t st) {
   if (!a) return CA_ERR_INVALID;
   if (a->q_work) return CA_ERR_INVALID;  // the library supplies the scratch
-  if (a->batch < 0 || a->n_active < 0 || a->n_head <= 0 || a->head_dim <= 0)
+  if (a->batch < 0 || a->n_active < 0 || a->n_head <= 0 || a->n_head_kv <= 0 ||
+      a->head_dim <= 0)
     return CA_ERR_INVALID;
-  const unsigned long long need = static_cast<unsigned long long>(a->batch) * a->n_active *
-                                  a->n_head * a->head_dim;
-  if (need > kNoAllocElems) return CA_ERR_SCRATCH;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
-  NoAllocSlot& slot = g_noalloc[dev];
-  std::call_once(slot.once, [&slot] {
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_qwork) == cudaSuccess && ptr) {
-      slot.ptr = ptr;
-      slot.rc = CA_OK;
-    }
-  });
-  if (slot.rc != CA_OK) return slot.rc;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(dev, &scratch);
+  if (rc != CA_OK) return rc;
   ca_block_args b = *a;
-  b.q_work = slot.ptr;
+  b.q_work = scratch;
+  // The scratch holds the rotated queries only when the pre-ops pass writes
+  // them; calls that rotate Q inside the attention kernel read none of it.
+  // The size test divides step by step so that no product can wrap.
+  if (!block_fuses_q(&b, block_vec(&b))) {
+    unsigned long long room = kNoAllocElems;
+    const int64_t f[4] = {a->batch, a->n_active, a->n_head, a->head_dim};
+    const bool empty = f[0] == 0 || f[1] == 0;
+    for (int i = 0; i < 4 && !empty; ++i) {
+      if (static_cast<unsigned long long>(f[i]) > room) return CA_ERR_SCRATCH;
+      room /= static_cast<unsigned long long>(f[i]);
+    }
+  }
   return block_impl(&b, st);
 }
 
@@ -652,7 +687,7 @@ int noalloc_impl(const ca_block_args* a, cudaStream_t st) {
 // gives up, stores CA_ERR_TIMEOUT in the device error word and the kernel
 // returns normally: the host sees the expiry through ca_device_status and
 // the context stays usable. No trap, fault or unbounded loop is involved.
-__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+__global__ void selftest_wait_kernel(uint64_t limit_ns, int* status) {
   __shared__ __align__(8) uint64_t never;
   const uint32_t bar = smem_u32(&never);
   if (threadIdx.x == 0) {
@@ -661,7 +696,7 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns) {
   }
   __syncthreads();
   bool dead = false;
-  mbar_wait_limit(bar, 0, dead, limit_ns);
+  mbar_wait_limit(bar, 0, dead, limit_ns, status);
 }
 
 }  // namespace
@@ -672,7 +707,14 @@ extern "C" {
 int ca_selftest_wait_timeout(int64_t limit_ns, void* stream) {
   if (limit_ns <= 0 || limit_ns > 1000000000ll) return CA_ERR_INVALID;
   ca::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<uint64_t>(limit_ns));
+      static_cast<uint64_t>(limit_ns), nullptr);
+  return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
+}
+
+int ca_selftest_wait_timeout_status(int64_t limit_ns, int32_t* status, void* stream) {
+  if (limit_ns <= 0 || limit_ns > 1000000000ll || !status) return CA_ERR_INVALID;
+  ca::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint64_t>(limit_ns), status);
   return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
 }
 
@@ -740,14 +782,5 @@ const char* ca_status_string(int status) {
 
 const char* ca_version(void) { return "canvas_attn 0.1.0 sm_100a"; }
 
-#ifdef CA_TRACE
-// Diagnostic builds only: copies the recorded event timestamps to `dst`.
-int ca_debug_trace(long long* dst) {
-  return cudaMemcpyFromSymbol(dst, ca::g_trace, sizeof(ca::g_trace)) == cudaSuccess ? 0 : -3;
-}
-int ca_debug_trace_w(long long* dst) {
-  return cudaMemcpyFromSymbol(dst, ca::g_trace_w, sizeof(ca::g_trace_w)) == cudaSuccess ? 0 : -3;
-}
-#endif
 
 }  // extern "C"

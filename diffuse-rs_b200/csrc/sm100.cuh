@@ -10,8 +10,9 @@
 
 namespace ca {
 
-// Device-side error word: a kernel whose bounded wait expires stores
-// CA_ERR_TIMEOUT (-4) here and leaves its loops instead of hanging the GPU.
+// Device-side error word of launches given no status word of their own: a
+// kernel whose bounded wait expires stores CA_ERR_TIMEOUT (-4) here (or in
+// the launch's own word) and leaves its loops instead of hanging the GPU.
 __device__ int g_device_error;
 
 constexpr int kErrTimeout = -4;
@@ -81,16 +82,17 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 }
 
 // Waits for the phase with the given parity to complete. Returns false (and
-// records the timeout in g_device_error) if it does not complete within
-// kWaitLimitNs, or immediately if *dead is already set by an earlier expiry.
+// records the timeout in *err, or in g_device_error when err is null) if it
+// does not complete within limit_ns, or immediately if `dead` is already set
+// by an earlier expiry.
 __device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, bool& dead,
-                                                uint64_t limit_ns) {
+                                                uint64_t limit_ns, int* err = nullptr) {
   if (dead) return false;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (!mbar_try_wait_sleep(bar, parity, 100000u)) {
     if (global_timer_ns() - t0 > limit_ns) {
-      atomicExch(&g_device_error, kErrTimeout);
+      atomicExch(err ? err : &g_device_error, kErrTimeout);
       dead = true;
       return false;
     }
@@ -98,8 +100,9 @@ __device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, b
   return true;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, bool& dead) {
-  return mbar_wait_limit(bar, parity, dead, kWaitLimitNs);
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, bool& dead,
+                                          int* err = nullptr) {
+  return mbar_wait_limit(bar, parity, dead, kWaitLimitNs, err);
 }
 
 // ---------------------------------------------------------------- TMA
@@ -272,13 +275,9 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn, i
 
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float ex2_approx(float x) {
-#ifdef CA_DIAG_NO_EX2
-  return fmaf(x, 0.0001f, 1.0f);
-#else
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-#endif
 }
 
 // 2^x on the FMA/ALU pipes, so that part of the softmax exponentials leave

@@ -115,6 +115,10 @@ typedef struct {
     int32_t precise;         /* 1: softmax weights enter the PV product as two bf16
                                 terms (hi + lo), ~2x the PV tensor work, error
                                 ~256x smaller; 0: one bf16 term (fastest) */
+    int32_t* status;         /* optional device int32: a bounded-wait expiry of this
+                                call's kernels is stored here (CA_ERR_TIMEOUT) instead
+                                of in the device-wide word that ca_device_status reads;
+                                the caller zeroes and reads it. NULL = device-wide word */
 } ca_dev_args;
 
 /*
@@ -158,6 +162,7 @@ typedef struct {
     float scale;
     float softcap;
     int32_t precise;           /* as ca_dev_args.precise */
+    int32_t* status;           /* as ca_dev_args.status */
 } ca_block_args;
 
 /*
@@ -183,16 +188,19 @@ int ca_attention_block_dev(const ca_block_args* a, void* stream);
  * output as usual but leaves a->q_work NULL: the normed, rotated queries go to
  * a scratch array compiled into the library (static device memory of
  * CA_NOALLOC_SCRATCH_BYTES = 16 MiB on every GPU that loads the library,
- * held until process exit). Requests needing more than that
- * (batch * n_active * n_head * head_dim * 2 bytes > 16 MiB) return
- * CA_ERR_SCRATCH before anything is launched. Nothing is allocated: no
- * cudaMalloc, no cudaFree, no allocating library call.
- * The first call on a device looks up the scratch array's device address
- * (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture. All calls share the one array, so calls whose
- * GPU work overlaps (other streams, other threads) race on it; the scratch
- * keeps the last call's values, which is harmless because every call writes
- * all of the scratch it reads before reading it.
+ * held until process exit). A call whose queries pass through the scratch
+ * (every call except head_dim-128 calls that rotate Q inside the attention
+ * kernel) and needs more than that (batch * n_active * n_head * head_dim * 2
+ * bytes > 16 MiB) returns CA_ERR_SCRATCH before anything is launched.
+ * Nothing is allocated: no cudaMalloc, no cudaFree, no allocating library
+ * call. Each call on a device looks up the scratch array's device address
+ * (cudaGetSymbolAddress) with that device current until one lookup has
+ * succeeded; make the first call before any stream capture. All calls share
+ * the one array and it keeps the last call's values. Calls that run one after
+ * another are unaffected, because each call writes all of the scratch it
+ * reads before reading it. Calls whose GPU work overlaps (other streams,
+ * other threads) race on the array and can return wrong outputs with no
+ * error status: do not overlap them.
  */
 int ca_attention_block_dev_noalloc(const ca_block_args* a, void* stream);
 #define CA_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
@@ -205,9 +213,12 @@ int ca_attention_block_dev_noalloc(const ca_block_args* a, void* stream);
 int ca_build_rope_table(float* out, int64_t max_seq_len, int64_t rope_dim, float theta,
                         const float* freq_factors);
 
-/* Reads and clears the device-side error word of the current device after
- * synchronising `stream`: CA_OK, or CA_ERR_TIMEOUT if a kernel's bounded wait
- * expired since the last call. */
+/* Reads and clears the device-wide error word of the current device after
+ * synchronising `stream`: CA_OK, or CA_ERR_TIMEOUT if the bounded wait of a
+ * kernel launched without a status word of its own (status == NULL) expired
+ * since the last call. The word is shared by every stream and thread of the
+ * process on that device; callers that need their own give each call a
+ * status word. */
 int ca_device_status(void* stream);
 
 /*
@@ -221,6 +232,11 @@ int ca_device_status(void* stream);
  * GPU that an expired wait is reported instead of hanging.
  */
 int ca_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
+/* The same self-test reporting to a caller-owned device int32 `status`
+ * (the per-call word of ca_dev_args.status) instead of the device-wide word:
+ * afterwards *status holds CA_ERR_TIMEOUT and ca_device_status is unaffected. */
+int ca_selftest_wait_timeout_status(int64_t limit_ns, int32_t* status, void* stream);
 
 /* Human-readable text of a ca_status. */
 const char* ca_status_string(int status);

@@ -51,3 +51,26 @@ def test_expiry_on_a_side_stream():
     ca.selftest_wait_timeout(5_000_000, stream=s)
     assert ca.device_status(stream=s) == ca.CA_ERR_TIMEOUT
     assert ca.device_status(stream=s) == ca.CA_OK
+
+
+def test_expiry_reported_to_a_per_call_status_word():
+    # A launch given its own status word reports there, not in the device-wide
+    # word: another stream polling ca_device_status neither sees nor clears it.
+    assert ca.device_status() == ca.CA_OK
+    word = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    ca.selftest_wait_timeout_status(5_000_000, word, stream=s)
+    s.synchronize()
+    assert ca.device_status() == ca.CA_OK
+    assert int(word.item()) == ca.CA_ERR_TIMEOUT
+    # An attention call with a status word leaves it at 0 when nothing expires.
+    word.zero_()
+    g = torch.Generator().manual_seed(12)
+    q = bf16_round(randn(g, 1, 40, 2, 64)).to(torch.bfloat16).cuda()
+    k = bf16_round(randn(g, 1, 40, 1, 64)).to(torch.bfloat16).cuda()
+    out = torch.empty((1, 40, 2, 64), dtype=torch.float32, device="cuda")
+    ca.attention_dev(q, k, k, out, batch=1, sq=40, sk=40, n_head=2, n_head_kv=1, head_dim=64,
+                     out_f32=True, scale=0.125, status=word)
+    torch.cuda.synchronize()
+    assert int(word.item()) == ca.CA_OK
+    assert ca.device_status() == ca.CA_OK

@@ -224,3 +224,77 @@ def test_block_with_cache_reuse_over_steps():
         # Cached rows are untouched; active rows now hold the new post-RoPE K/V.
         after_k = cache_k.float().cpu().numpy()
         np.testing.assert_array_equal(after_k[:, cached], before_k[:, cached])
+
+
+def _norm_v_heads(v, hd, eps):
+    """Gemma's unweighted RMSNorm of every V head (forward.rs:304-308,
+    rms_norm_noscale ops.rs:117-124), one head_dim chunk at a time."""
+    v = np.array(v, np.float32).reshape(-1, hd)
+    return np.concatenate([orc.rms_norm_noscale(row, eps) for row in v])
+
+
+@pytest.mark.parametrize("hd,rope_dim,v_norm,qk_norm,unaligned,S", [
+    (192, 192, True, True, False, 300),    # head_dim outside {64,128,256}: scalar pre-ops
+    (80, 80, True, True, False, 300),      # head_dim 80 (padded to 128 in the attention tile)
+    (128, 40, False, True, False, 300),    # rope_dim % 16 != 0: scalar pre-ops
+    (128, 128, True, False, True, 600),    # Q/K/V 2 bytes off 16-byte alignment: scalar pre-ops
+    (128, 128, True, True, False, 600),    # V norm with the Q pre-ops inside the attention kernel
+    (128, 128, True, True, False, 300),    # V norm in the vectorised token kernel
+    (256, 256, True, True, False, 300),    # V norm in the lane-paired head_dim-256 kernel
+    (64, 32, True, True, False, 300),      # partial rotation in the head_dim-64 token kernel
+])
+def test_block_pre_ops_variants(hd, rope_dim, v_norm, qk_norm, unaligned, S):
+    """Every form of the pre-ops pass against the reference op order
+    (forward.rs:296-310): QK-norm -> Gemma V norm -> RoPE -> cache store ->
+    attention."""
+    B, H, Hkv = 2, 4, 2
+    eps, theta = 1e-6, 10000.0
+    g = torch.Generator().manual_seed(hd * 7 + rope_dim + S)
+    q = bf16_round(randn(g, B, S, H, hd))
+    k = bf16_round(randn(g, B, S, Hkv, hd))
+    v = bf16_round(randn(g, B, S, Hkv, hd))
+    wq = torch.rand(hd, generator=g) + 0.5 if qk_norm else None
+    wk = torch.rand(hd, generator=g) + 0.5 if qk_norm else None
+    rope = ca.build_rope_cache(4096, rope_dim, theta)
+
+    def dev(x):
+        x = x.to(torch.bfloat16)
+        if not unaligned:
+            return x.cuda()
+        flat = torch.empty(x.numel() + 8, dtype=torch.bfloat16, device="cuda")
+        view = flat[1:1 + x.numel()].view(x.shape)  # 2 bytes past a 16-byte boundary
+        view.copy_(x.cuda())
+        assert view.data_ptr() % 16 == 2
+        return view
+
+    pos = torch.arange(S, dtype=torch.int32).repeat(B, 1)
+    cache_k = torch.zeros(B, S, Hkv, hd, dtype=torch.bfloat16, device="cuda")
+    cache_v = torch.zeros_like(cache_k)
+    q_work = torch.empty(B, S, H, hd, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(B, S, H, hd, device="cuda")
+    ca.attention_block_dev(dev(q), dev(k), dev(v), batch=B, n_active=S, active_pos=pos.cuda(),
+                           rope=torch.from_numpy(rope).cuda(), rope_len=4096, rope_dim=rope_dim,
+                           cache_k=cache_k, cache_v=cache_v, n_total=S, q_work=q_work, out=out,
+                           n_head=H, n_head_kv=Hkv, head_dim=hd,
+                           q_norm_w=None if wq is None else wq.cuda(),
+                           k_norm_w=None if wk is None else wk.cuda(), v_norm=v_norm,
+                           rms_eps=eps, out_f32=True, scale=hd ** -0.5, precise=True)
+    torch.cuda.synchronize()
+    assert ca.device_status() == ca.CA_OK
+    got = out.cpu().numpy()
+    what = f"pre-ops hd={hd} rope_dim={rope_dim} v_norm={v_norm} unaligned={unaligned}"
+    for b in range(B):
+        qq, kk, vv = _oracle_block(q[b].numpy().reshape(-1), k[b].numpy().reshape(-1),
+                                   v[b].numpy().reshape(-1), np.arange(S),
+                                   None if wq is None else wq.numpy(),
+                                   None if wk is None else wk.numpy(), rope, rope_dim, H, Hkv,
+                                   hd, eps)
+        if v_norm:
+            vv = bf16_round(torch.from_numpy(_norm_v_heads(vv, hd, eps))).numpy()
+        # The cache holds the bf16 post-RoPE K and the bf16 (normed) V.
+        np.testing.assert_allclose(cache_k[b].float().cpu().numpy().reshape(-1), kk,
+                                   atol=1e-2, rtol=1e-2, err_msg=what)
+        np.testing.assert_allclose(cache_v[b].float().cpu().numpy().reshape(-1), vv,
+                                   atol=1e-2, rtol=1e-2, err_msg=what)
+        ref = oracle_attention(qq, kk, vv, nq=S, nk=S, h=H, hkv=Hkv, hd=hd, scale=hd ** -0.5)
+        check_close(got[b], ref, H, hd, what=f"{what} b={b}")
