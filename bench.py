@@ -666,9 +666,11 @@ def run_ours(args, cfg):
             c = CONFIGS[name]
             w2 = Workload(c, dev, seed=99)
             fl2 = w2.input_bytes() < 2 * L2_BYTES
+            if fl2 and scratch is None:
+                scratch = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
             for i in range(3):
                 w2.step(i)  # writes q_work (the rotated Q the kernel-alone run reads)
-            ms = kernel_ms(w2, fl2, scratch if fl2 else None, reps)
+            ms = kernel_ms(w2, fl2, scratch, reps)
             if name == "c5":  # sliding-window layers and the global layer apart
                 slide = [k for k, (w, _) in enumerate(c["layers"]) if w is not None]
                 glob = [k for k, (w, _) in enumerate(c["layers"]) if w is None]

@@ -83,7 +83,8 @@ struct FwdParams {
 enum FwdMode { kSplit = 0, kAlt = 1 };
 
 
-template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_, int STK_ = ST_>
+template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_, int STK_ = ST_, int KSUB_ = 1,
+          int VSUB_ = 1, int OS_ = 1>
 struct FwdCfg {
   static constexpr int HDP = HDP_;  // head_dim padded to a multiple of 64
   static constexpr int BN = BN_;    // keys per tile
@@ -96,6 +97,15 @@ struct FwdCfg {
   static constexpr bool ALT = MODE == kAlt;
   static constexpr bool SPLIT = MODE == kSplit;
   static constexpr int kPTerms = PRECISE ? 2 : 1;
+  // Wide heads (head_dim > 256): OS CTAs share one Q tile, each computing
+  // S = Q K^T over the whole head and owning HDO = HDP / OS columns of O
+  // (an fp32 O of 512 columns would fill TMEM). K tiles then stream as KSUB
+  // units of HDP / KSUB dims and V tiles as VSUB units of BN / VSUB keys, so
+  // that the whole Q tile stays resident beside rings of several units.
+  static constexpr int OS = OS_;
+  static constexpr int HDO = HDP / OS;  // O columns of this CTA
+  static constexpr int KSUB = KSUB_;
+  static constexpr int VSUB = VSUB_;
   // S buffers in TMEM (P overwrites S in place). kSplit keeps one O, which
   // leaves room for a third buffer: S runs two tiles ahead of the softmax.
   static constexpr int SB = SPLIT ? 3 : 2;
@@ -103,16 +113,21 @@ struct FwdCfg {
   static constexpr int kQChunk = 128 * 128;
   static constexpr int kKChunk = BN * 128;
   static constexpr int kQBytes = kChunks * kQChunk;
-  static constexpr int kKVBytes = kChunks * kKChunk;
+  static constexpr int kKUnitChunks = kChunks / KSUB;   // atoms per K unit
+  static constexpr int kKUnitBytes = kKUnitChunks * kKChunk;
+  static constexpr int kVRows = BN / VSUB;              // keys per V unit
+  static constexpr int kVChunk = kVRows * 128;
+  static constexpr int kOChunks = HDO / 64;             // V atoms this CTA reads
+  static constexpr int kVUnitBytes = kOChunks * kVChunk;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;
-  static constexpr int kOffV = kOffK + STK * kKVBytes;
-  static constexpr int kOffBar = kOffV + ST * kKVBytes;
+  static constexpr int kOffV = kOffK + STK * kKUnitBytes;
+  static constexpr int kOffBar = kOffV + ST * kVUnitBytes;
   // Barriers. K and V stages are released separately: a K stage as soon as
   // its Q K^T MMA completes, a V stage when its P V MMA(s) complete.
   static constexpr int kBarQ = 0;
-  static constexpr int kBarK = 1;             // [STK] K tile landed
-  static constexpr int kBarV = kBarK + STK;   // [ST] V tile landed
+  static constexpr int kBarK = 1;             // [STK] K unit landed
+  static constexpr int kBarV = kBarK + STK;   // [ST] V unit landed
   static constexpr int kBarKE = kBarV + ST;   // [STK] K stage free
   static constexpr int kBarVE = kBarKE + STK; // [ST] V stage free
   static constexpr int kBarS = kBarVE + ST;   // [SB] S buffer holds Q K^T
@@ -135,13 +150,19 @@ struct FwdCfg {
   static constexpr int kTmemCols = 512;
   static constexpr int kOCol = SB * BN;  // O accumulator(s) after the S buffers
   static constexpr uint32_t kIdescS = umma_idesc_bf16(128, BN, 0, 0);
-  static constexpr uint32_t kIdescO = umma_idesc_bf16(128, HDP, 0, 1);
-  static_assert(kOCol + (SPLIT ? 1 : 2) * HDP <= kTmemCols, "TMEM budget");
+  static constexpr uint32_t kIdescO = umma_idesc_bf16(128, HDO, 0, 1);
+  static_assert(kOCol + (SPLIT ? 1 : 2) * HDO <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
-  static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 256, "tile shape");
-  // The epilogue stages the output tile (up to fp32) in the idle K/V rings.
+  static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 512, "tile shape");
+  static_assert(HDO % 64 == 0 && HDO <= 256 && kChunks % KSUB == 0 && BN % (16 * VSUB) == 0,
+                "unit shape");
+  static_assert(OS == 1 || SPLIT, "wide heads use the split softmax");
+  // The epilogue stages the output tile (up to fp32) in shared memory that
+  // is idle by then: the K/V rings, or for wide heads the Q tile.
   static constexpr int kStageChunk = 128 * 128;  // one 128-byte column chunk, 128 rows
-  static_assert(128 * HDP * 4 <= (STK + ST) * kKVBytes, "output staging fits in the K/V rings");
+  static constexpr int kOffStage = OS > 1 ? kOffQ : kOffK;
+  static constexpr int kStageBytes = OS > 1 ? kQBytes : STK * kKUnitBytes + ST * kVUnitBytes;
+  static_assert(128 * HDO * 4 <= kStageBytes, "output staging fits in idle shared memory");
 };
 
 // visible(): src/model/attention.rs:35-57 on int32 positions.
@@ -488,7 +509,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int qtile = blockIdx.x;  // query tile
+  const int qtile = blockIdx.x / C::OS;  // query tile
+  const int ohalf = blockIdx.x % C::OS;  // which HDO columns of O (wide heads)
   const int kvh = blockIdx.y;
   const int b = blockIdx.z;
 
@@ -504,6 +526,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * i; };
   uint16_t* list = reinterpret_cast<uint16_t*>(smem + C::kOffList);
   int* misc = reinterpret_cast<int*>(smem + C::kOffMisc);  // [0]=tmem base [1]=n_tiles
+  // K unit u (tile u / KSUB, head_dim atoms of part u % KSUB) of the tile at
+  // key row `row`, into K stage s; V unit u (keys (u % VSUB) * kVRows.. of
+  // the tile, this CTA's HDO columns) into V stage s.
+  auto load_k_unit = [&](int u, int s, int row) {
+    const int part = u % C::KSUB;
+    mbar_arrive_expect_tx(bar(C::kBarK + s), C::kKUnitBytes);
+#pragma unroll
+    for (int c = 0; c < C::kKUnitChunks; ++c)
+      tma_load_3d(sK + s * C::kKUnitBytes + c * C::kKChunk, &tm_k, bar(C::kBarK + s),
+                  (part * C::kKUnitChunks + c) * 64, kvh, row);
+  };
+  auto load_v_unit = [&](int u, int s, int row) {
+    const int part = u % C::VSUB;
+    mbar_arrive_expect_tx(bar(C::kBarV + s), C::kVUnitBytes);
+#pragma unroll
+    for (int c = 0; c < C::kOChunks; ++c)
+      tma_load_3d(sV + s * C::kVUnitBytes + c * C::kVChunk, &tm_v, bar(C::kBarV + s),
+                  ohalf * C::HDO + c * 64, kvh, row + part * C::kVRows);
+  };
 
   if (tid == 0) {
     mbar_init(bar(C::kBarQ), 1);
@@ -535,22 +576,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // TMEM allocation (the producers continue from stage STK / ST).
     if (!p.any_mask) {
       const int n_kt = (k_len + BN - 1) / BN;
-      const int ek = min(STK, n_kt), ev = min(ST, n_kt);
-      for (int jj = 0; jj < ek || jj < ev; ++jj) {
-        if (jj < ek) {
-          mbar_arrive_expect_tx(bar(C::kBarK + jj), C::kKVBytes);
-#pragma unroll
-          for (int c = 0; c < C::kChunks; ++c)
-            tma_load_3d(sK + jj * C::kKVBytes + c * C::kKChunk, &tm_k, bar(C::kBarK + jj),
-                        c * 64, kvh, k_beg + jj * BN);
-        }
-        if (jj < ev) {
-          mbar_arrive_expect_tx(bar(C::kBarV + jj), C::kKVBytes);
-#pragma unroll
-          for (int c = 0; c < C::kChunks; ++c)
-            tma_load_3d(sV + jj * C::kKVBytes + c * C::kKChunk, &tm_v, bar(C::kBarV + jj),
-                        c * 64, kvh, k_beg + jj * BN);
-        }
+      const int ek = min(STK, n_kt * C::KSUB), ev = min(ST, n_kt * C::VSUB);
+      for (int u = 0; u < ek || u < ev; ++u) {
+        if (u < ek) load_k_unit(u, u, k_beg + (u / C::KSUB) * BN);
+        if (u < ev) load_v_unit(u, u, k_beg + (u / C::VSUB) * BN);
       }
     }
   }
@@ -574,25 +603,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // one warp their diverged waits delayed each other's loads.
     if (lane == 0) {
       const bool is_k = warp == 0;
-      const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
-      const uint32_t ring = is_k ? sK : sV;
       const int full = is_k ? C::kBarK : C::kBarV;
       const int empty = is_k ? C::kBarKE : C::kBarVE;
-      const int NS = is_k ? STK : ST;  // stages of this ring
-      for (int j = p.any_mask ? 0 : min(NS, n); j < n; ++j) {
-        const int s = j % NS;
-        if (j >= NS && !mbar_wait(bar(empty + s), ((j / NS) - 1) & 1, dead, p.err)) break;
-        const int krow = k_beg + (list[j] & 0x3fff) * BN;
-        mbar_arrive_expect_tx(bar(full + s), C::kKVBytes);
-#pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(ring + s * C::kKVBytes + c * C::kKChunk, tm, bar(full + s), c * 64, kvh,
-                      krow);
+      const int NS = is_k ? STK : ST;              // stages of this ring
+      const int SUB = is_k ? C::KSUB : C::VSUB;    // units per key tile
+      const int U = n * SUB;
+      for (int u = p.any_mask ? 0 : min(NS, U); u < U; ++u) {
+        const int s = u % NS;
+        if (u >= NS && !mbar_wait(bar(empty + s), ((u / NS) - 1) & 1, dead, p.err)) break;
+        const int row = k_beg + (list[u / SUB] & 0x3fff) * BN;
+        if (is_k) load_k_unit(u, s, row);
+        else load_v_unit(u, s, row);
       }
       // Leave no bulk copy in flight: wait (bounded) for the last loads.
       bool d2 = false;
       if (is_k) mbar_wait(bar(C::kBarQ), 0, d2, p.err);
-      for (int j = max(0, n - NS); j < n; ++j) mbar_wait(bar(full + j % NS), (j / NS) & 1, d2, p.err);
+      for (int u = max(0, U - NS); u < U; ++u)
+        mbar_wait(bar(full + u % NS), (u / NS) & 1, d2, p.err);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -605,49 +632,71 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // waits for it here (no later P V on that barrier is issued yet);
       // kSplit issues S[j] after P V[j - 2], whose issue already waited for
       // P V[j - 3].
+      // K arrives in KSUB units per tile (one unit for head_dim <= 256), each
+      // released as soon as its share of the Q K^T MMAs completes.
       auto issue_s = [&](int j) -> bool {
-        const int s = j % STK;
         const int sb = j % C::SB;
-        if (!mbar_wait(bar(C::kBarK + s), (j / STK) & 1, dead, p.err)) return false;
-        if (ALT && j >= 2 && !mbar_wait(bar(C::kBarO + og(j - 2)), ouse(j - 2) & 1, dead, p.err))
-          return false;
-        tc_fence_after();
-        const uint32_t kbase = sK + s * C::kKVBytes;
+        constexpr int KK = HDP / 16 / C::KSUB;  // 16-wide k-steps per K unit
 #pragma unroll
-        for (int kk = 0; kk < HDP / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(sQ + (kk >> 2) * C::kQChunk + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(kbase + (kk >> 2) * C::kKChunk + (kk & 3) * 32, 16, 1024);
-          umma_ss(tmem + sb * BN, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
+        for (int part = 0; part < C::KSUB; ++part) {
+          const int u = j * C::KSUB + part;
+          const int s = u % STK;
+          if (!mbar_wait(bar(C::kBarK + s), (u / STK) & 1, dead, p.err)) return false;
+          if (part == 0 && ALT && j >= 2 &&
+              !mbar_wait(bar(C::kBarO + og(j - 2)), ouse(j - 2) & 1, dead, p.err))
+            return false;
+          tc_fence_after();
+          const uint32_t kbase = sK + s * C::kKUnitBytes;
+#pragma unroll
+          for (int k2 = 0; k2 < KK; ++k2) {
+            const int kk = part * KK + k2;
+            const uint64_t a =
+                umma_desc_sw128(sQ + (kk >> 2) * C::kQChunk + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd =
+                umma_desc_sw128(kbase + (k2 >> 2) * C::kKChunk + (k2 & 3) * 32, 16, 1024);
+            umma_ss(tmem + sb * BN, a, bd, C::kIdescS, kk > 0 ? 1u : 0u);
+          }
+          if (part == C::KSUB - 1) umma_commit(bar(C::kBarS + sb));
+          umma_commit(bar(C::kBarKE + s));
         }
-        umma_commit(bar(C::kBarS + sb));
-        umma_commit(bar(C::kBarKE + s));
         return true;
       };
-      // O[g] += P[i] V_i, P read from TMEM (S buffer i & 1, 16 columns per
-      // 16 keys: hi terms in the first 8, lo terms in the last 8).
+      // O[g] += P[i] V_i, P read from TMEM (S buffer i % SB, 16 columns per
+      // 16 keys: hi terms in the first 8, lo terms in the last 8). V arrives
+      // in VSUB units of kVRows keys per tile.
       auto issue_pv = [&](int i) -> bool {
-        const int s = i % ST;
         const int g = og(i), use = ouse(i);
-        if (!mbar_wait(bar(C::kBarV + s), (i / ST) & 1, dead, p.err)) return false;
-        if (!mbar_wait(bar(C::kBarP + g), use & 1, dead, p.err)) return false;
-        // kSplit: P V[i - 1] done (frees the buffer S[i + 2] takes). Checked
-        // before P V[i] is issued, so the O barrier is at most one phase on.
-        if (SPLIT && i > 0 && !mbar_wait(bar(C::kBarO), (i - 1) & 1, dead, p.err)) return false;
-        tc_fence_after();
-        const uint32_t vbase = sV + s * C::kKVBytes;
+        constexpr int KK = BN / 16 / C::VSUB;  // 16-key steps per V unit
         const uint32_t pcol = tmem + (i % C::SB) * BN;
-        const uint32_t dst = tmem + C::kOCol + g * HDP;
+        const uint32_t dst = tmem + C::kOCol + g * C::HDO;
 #pragma unroll
-        for (int term = 0; term < C::kPTerms; ++term) {
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(vbase + kk * 2048, C::kKChunk, 1024);
-            umma_ts(dst, pcol + kk * 16 + term * 8, bd, C::kIdescO,
-                    (use > 0 || kk > 0 || term > 0) ? 1u : 0u);
+        for (int part = 0; part < C::VSUB; ++part) {
+          const int u = i * C::VSUB + part;
+          const int s = u % ST;
+          if (!mbar_wait(bar(C::kBarV + s), (u / ST) & 1, dead, p.err)) return false;
+          if (part == 0) {
+            if (!mbar_wait(bar(C::kBarP + g), use & 1, dead, p.err)) return false;
+            // kSplit: P V[i - 1] done (frees the buffer S[i + 2] takes).
+            // Checked before P V[i] is issued, so the O barrier is at most
+            // one phase on.
+            if (SPLIT && i > 0 && !mbar_wait(bar(C::kBarO), (i - 1) & 1, dead, p.err))
+              return false;
           }
+          tc_fence_after();
+          const uint32_t vbase = sV + s * C::kVUnitBytes;
+#pragma unroll
+          for (int term = 0; term < C::kPTerms; ++term) {
+#pragma unroll
+            for (int k2 = 0; k2 < KK; ++k2) {
+              const int kk = part * KK + k2;
+              const uint64_t bd = umma_desc_sw128(vbase + k2 * 2048, C::kVChunk, 1024);
+              umma_ts(dst, pcol + kk * 16 + term * 8, bd, C::kIdescO,
+                      (use > 0 || kk > 0 || term > 0) ? 1u : 0u);
+            }
+          }
+          if (part == C::VSUB - 1) umma_commit(bar(C::kBarO + g));
+          umma_commit(bar(C::kBarVE + s));
         }
-        umma_commit(bar(C::kBarO + g));
-        umma_commit(bar(C::kBarVE + s));
         return true;
       };
       // Order: S[0], S[1], then per tile j: P V[j] once P[j] is written,
@@ -670,7 +719,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // Warps 3..10: warp w reaches TMEM lanes 32 (w % 4) .. +31, so each lane
     // quarter q has two warps, one per group (grp 0: warps 3-6, 1: 7-10).
     constexpr int SC = SPLIT ? BN / 2 : BN;    // S columns per thread per tile
-    constexpr int OC = SPLIT ? HDP / 2 : HDP;  // O columns this group owns
+    constexpr int OC = SPLIT ? C::HDO / 2 : C::HDO;  // O columns this group owns
     const int wq = warp & 3;
     const int grp = (warp - 3) >> 2;
     const int r = wq * 32 + lane;
@@ -1062,10 +1111,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int head = kvh * p.G + (r % p.G);
     // Columns this warp writes: kAlt half of the columns from both
     // accumulators; kSplit its own half.
-    constexpr int WC = HDP / 2;
+    constexpr int WC = C::HDO / 2;
     const int col0 = grp * WC;
-    const uint32_t o_me = ALT ? C::kOCol + grp * HDP + col0 : o_own;
-    const uint32_t o_ot = C::kOCol + (grp ^ 1) * HDP + col0;
+    const uint32_t o_me = ALT ? C::kOCol + grp * C::HDO + col0 : o_own;
+    const uint32_t o_ot = C::kOCol + (grp ^ 1) * C::HDO + col0;
+    const int ocol = ohalf * C::HDO;  // this CTA's first output column
 #pragma unroll 1
     for (int c = 0; c < WC / 32; ++c) {
       const int col_base = col0 + c * 32;
@@ -1090,7 +1140,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // Stage row r in 128-byte column chunks, 16-byte units XOR-swizzled
         // by r & 7 (the tensor map's 128-byte swizzle); rows past the
         // sequence end and columns past head_dim are clipped by the store.
-        uint8_t* stg = smem + C::kOffK;
+        uint8_t* stg = smem + C::kOffStage;
         if (p.out_f32) {
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
@@ -1126,7 +1176,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                               static_cast<int64_t>(head) * p.hd;
 #pragma unroll
         for (int g8 = 0; g8 < 4; ++g8) {
-          const int col = col_base + g8 * 8;
+          const int col = ocol + col_base + g8 * 8;
           if (col < p.hd) {
             float w8[8];
 #pragma unroll
@@ -1153,9 +1203,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       named_bar_sync(2, 256);
       if (warp == 3 && lane == 0) {
         const int inner = p.out_f32 ? 32 : 64;  // elements per 128-byte chunk
-        for (int ci = 0; ci * inner < p.hd; ++ci)
-          tma_store_4d(&tm_o, smem_u32(smem + C::kOffK + ci * C::kStageChunk), ci * inner,
-                       kvh * p.G, t0, b);
+        for (int ci = 0; ci * inner < C::HDO && ocol + ci * inner < p.hd; ++ci)
+          tma_store_4d(&tm_o, smem_u32(smem + C::kOffStage + ci * C::kStageChunk),
+                       ocol + ci * inner, kvh * p.G, t0, b);
         bulk_commit_group();
         bulk_wait_group_read0();
       }

@@ -105,7 +105,8 @@ struct Launch {
     int rc;
     if ((rc = make_tmap(&tq, a->q, hd, p->n_head, total_q, qrs, p->G, p->QT)) != CA_OK) return rc;
     if ((rc = make_tmap(&tk, a->k, hd, p->n_head_kv, tk_rows, krs, 1, C::BN)) != CA_OK) return rc;
-    if ((rc = make_tmap(&tv, a->v, hd, p->n_head_kv, tk_rows, krs, 1, C::BN)) != CA_OK) return rc;
+    if ((rc = make_tmap(&tv, a->v, hd, p->n_head_kv, tk_rows, krs, 1, C::kVRows)) != CA_OK)
+      return rc;
     // Uniform batches store O through a tensor map (the map clips at each
     // sequence's end); otherwise the kernel stores rows itself.
     FwdParams pl = *p;
@@ -126,7 +127,7 @@ struct Launch {
       attr_done[dev] = true;
     }
     const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
-    dim3 grid(n_qtiles, p->n_head_kv, p->batch);
+    dim3 grid(n_qtiles * C::OS, p->n_head_kv, p->batch);
     attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, to, pl);
     return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
   }
@@ -156,7 +157,7 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
   const int H = a->n_head, Hkv = a->n_head_kv, hd = a->head_dim;
   if (H <= 0 || Hkv <= 0 || hd <= 0 || a->batch < 0) return CA_ERR_INVALID;
   if (H % Hkv != 0) return CA_ERR_INVALID;
-  if (hd % 8 != 0 || hd > 256) return CA_ERR_UNSUPPORTED;
+  if (hd % 8 != 0 || hd > 512) return CA_ERR_UNSUPPORTED;
   const int G = H / Hkv;
   if (G > 128) return CA_ERR_UNSUPPORTED;
   if (a->batch == 0) return CA_OK;
@@ -232,6 +233,17 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
   // three at head_dim 128 (970 vs 949 TFLOP/s at B8 S4096 H16; the smaller
   // shared-memory carve-out leaves more L1), and at head_dim 64 and 192. (kSplit with three S buffers
   // at head_dim 128 measured 746 vs 823 TFLOP/s for kAlt.)
+  // head_dim 257..512: two CTAs per Q tile, each owning half of O's columns
+  // (TMEM cannot hold a 512-column fp32 O beside the S buffers); K streams in
+  // units of 128 head_dim columns and V in units of 32 keys, so the whole
+  // Q tile (up to 128 KB) stays resident.
+  if (hdp > 256) {
+    if (hdp <= 384)
+      return a->precise ? L.run<FwdCfg<384, 64, 2, true, kSplit, 3, 3, 2, 2>>()
+                        : L.run<FwdCfg<384, 64, 2, false, kSplit, 3, 3, 2, 2>>();
+    return a->precise ? L.run<FwdCfg<512, 64, 2, true, kSplit, 3, 4, 2, 2>>()
+                      : L.run<FwdCfg<512, 64, 2, false, kSplit, 3, 4, 2, 2>>();
+  }
   if (a->precise) {
     if (hdp == 64) return L.run<FwdCfg<64, 128, 2, true, kAlt>>();
     if (hdp == 128) return L.run<FwdCfg<128, 128, 2, true, kAlt>>();

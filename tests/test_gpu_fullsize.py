@@ -113,3 +113,11 @@ def test_c5_fullsize_rows(window, theta):
     d = _block(5, 4, 8192, 8192, 0, 16, 8, 256, theta, True, window=window, softcap=50.0,
                scale=256 ** -0.5)
     _check_rows(d, 1, 128, seed=7)
+
+
+def test_gemma_global_layer_head_dim_512_fullsize_rows():
+    # c5's shape with the real DiffusionGemma global-layer heads: B4 S8192,
+    # 16 query heads over 2 kv heads (GQA group 8), head_dim 512, QK-norm,
+    # soft-cap 50, scale 1.0 (forward.rs:341).
+    d = _block(6, 4, 8192, 8192, 0, 16, 2, 512, 1e6, True, softcap=50.0, scale=1.0)
+    _check_rows(d, 2, 96, seed=11)

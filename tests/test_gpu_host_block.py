@@ -41,12 +41,6 @@ def host_call(c, q, k, v):
 def test_host_entry_on_golden_cases(name):
     c = CASES[name]
     nq, nk, h, hkv, hd = (int(x) for x in c["dims"])
-    if hd > 256:
-        # head_dim 320 is valid for the reference, unsupported by this build.
-        with pytest.raises(ca.CaError) as e:
-            host_call(c, c["q"], c["k"], c["v"])
-        assert e.value.status == ca.CA_ERR_UNSUPPORTED
-        return
     q, k, v = (bf16_round(torch.from_numpy(c[x])).numpy() for x in ("q", "k", "v"))
     got = host_call(c, q, k, v)
     win, cp = int(c["window"]), int(c["causal_prefix"])
@@ -242,6 +236,8 @@ def _norm_v_heads(v, hd, eps):
     (128, 128, True, True, False, 300),    # V norm in the vectorised token kernel
     (256, 256, True, True, False, 300),    # V norm in the lane-paired head_dim-256 kernel
     (64, 32, True, True, False, 300),      # partial rotation in the head_dim-64 token kernel
+    (512, 512, True, True, False, 300),    # Gemma global layer: head_dim 512
+    (320, 256, False, True, False, 200),   # head_dim 320 with partial rotation
 ])
 def test_block_pre_ops_variants(hd, rope_dim, v_norm, qk_norm, unaligned, S):
     """Every form of the pre-ops pass against the reference op order

@@ -55,6 +55,12 @@ def ref_batched(q, k, v, *, h, hkv, hd, scale, **kw):
     (1, 64, 200, 2, 2, 192),
     (1, 100, 150, 2, 1, 72),    # head_dim padded to 128 by the TMA zero fill
     (1, 40, 4128, 32, 8, 128),  # c4-like: 32 queries x 4 heads per tile
+    # Wide heads (DiffusionGemma global layers: head_dim 512, 16/2 heads):
+    # two CTAs per Q tile, each owning half of O's columns.
+    (1, 130, 300, 16, 2, 512),
+    (2, 100, 257, 4, 1, 320),   # head_dim 320 runs the 384-column tile
+    (1, 64, 129, 2, 2, 264),    # 264: the second CTA's columns are mostly padding
+    (1, 33, 520, 8, 2, 384),
 ])
 @pytest.mark.parametrize("precise", [False, True])
 def test_dense_matches_oracle(B, Sq, Sk, H, Hkv, hd, precise):
@@ -150,3 +156,52 @@ def test_varlen_batch():
             check_close(got[oq:oq + lq], ref, H, hd, what=f"varlen {lq}x{lk}")
         oq += lq
         ok += lk
+
+
+@pytest.mark.parametrize("hd", [320, 512])
+def test_wide_heads_with_masks_bf16_out_and_varlen(hd):
+    # Gemma global-layer form: scale 1.0 and soft-cap; plus a sliding window,
+    # a causal prefix, bf16 output and a varlen batch at head_dim > 256.
+    g = torch.Generator().manual_seed(hd)
+    S, H, Hkv = 300, 8, 1
+    q, k, v = randn(g, 1, S, H, hd, scale=0.05), randn(g, 1, S, Hkv, hd), randn(g, 1, S, Hkv, hd)
+    got = dev_attention(q, k, v, h=H, hkv=Hkv, hd=hd, scale=1.0, softcap=50.0, precise=True)
+    ref = ref_batched(q, k, v, h=H, hkv=Hkv, hd=hd, scale=1.0, softcap=50.0)
+    check_close(got.numpy(), ref, H, hd, what=f"hd {hd} soft-cap")
+    got = dev_attention(q, k, v, h=H, hkv=Hkv, hd=hd, scale=hd ** -0.5, sliding_window=40,
+                        causal_prefix=100, precise=True)
+    ref = ref_batched(q, k, v, h=H, hkv=Hkv, hd=hd, scale=hd ** -0.5, sliding_window=40,
+                      causal_prefix=100)
+    check_close(got.numpy(), ref, H, hd, what=f"hd {hd} window + prefix")
+    got = dev_attention(q, k, v, h=H, hkv=Hkv, hd=hd, scale=hd ** -0.5, out_f32=False)
+    ref = ref_batched(q, k, v, h=H, hkv=Hkv, hd=hd, scale=hd ** -0.5)
+    check_close(got.numpy(), ref, H, hd, atol=6e-3, what=f"hd {hd} bf16 out")
+    lens_q, lens_k = [70, 0, 130], [90, 20, 130]
+    tq, tk = sum(lens_q), sum(lens_k)
+    q, k, v = randn(g, tq, H, hd), randn(g, tk, Hkv, hd), randn(g, tk, Hkv, hd)
+    cu_q = torch.tensor(np.cumsum([0] + lens_q), dtype=torch.int32, device="cuda")
+    cu_k = torch.tensor(np.cumsum([0] + lens_k), dtype=torch.int32, device="cuda")
+    out = torch.zeros(tq, H, hd, device="cuda")
+    ca.attention_dev(*(x.to(torch.bfloat16).cuda() for x in (q, k, v)), out,
+                     batch=len(lens_q), sq=0, sk=0, cu_q=cu_q, cu_k=cu_k, max_sq=max(lens_q),
+                     total_q=tq, total_k=tk, n_head=H, n_head_kv=Hkv, head_dim=hd,
+                     out_f32=True, scale=hd ** -0.5, precise=True)
+    torch.cuda.synchronize()
+    assert ca.device_status() == ca.CA_OK
+    got = out.cpu().numpy()
+    oq = ok = 0
+    for lq, lk in zip(lens_q, lens_k):
+        if lq:
+            ref = oracle_attention(bf16_round(q[oq:oq + lq]), bf16_round(k[ok:ok + lk]),
+                                   bf16_round(v[ok:ok + lk]), nq=lq, nk=lk, h=H, hkv=Hkv,
+                                   hd=hd, scale=hd ** -0.5)
+            check_close(got[oq:oq + lq], ref, H, hd, what=f"hd {hd} varlen {lq}x{lk}")
+        oq += lq
+        ok += lk
+
+
+def test_head_dim_beyond_512_is_unsupported():
+    x = torch.zeros(8, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ca.CaError) as e:
+        ca.attention_dev(x, x, x, x, batch=1, sq=1, sk=1, n_head=1, n_head_kv=1, head_dim=520)
+    assert e.value.status == ca.CA_ERR_UNSUPPORTED
