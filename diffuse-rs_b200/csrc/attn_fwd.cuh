@@ -1079,6 +1079,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       dead = __any_sync(0xffffffffu, dead);
       tc_fence_after();
     }
+    // Wide heads stage the output in the Q tile: its load must have landed
+    // (a tile with no visible key issues no MMA that would have waited).
+    if constexpr (C::kOffStage == C::kOffQ) {
+      if (p.tma_out && n == 0) mbar_wait(bar(C::kBarQ), 0, dead, p.err);
+    }
     bool have = n > 0 && !dead;
     float s_me = 1.f, s_ot = 0.f, inv = __int_as_float(0x7fc00000);
     const int n_me = ALT ? (grp == 0 ? (n + 1) / 2 : n / 2) : n;
