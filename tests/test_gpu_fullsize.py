@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 
 def _block(cfg_seed, B, na, n_total, start, H, Hkv, hd, theta, qk_norm, window=None,
-           softcap=0.0, scale=None):
+           softcap=0.0, scale=None, precise=False):
     """Runs one fused block on the GPU; returns inputs (fp32 CPU) and output."""
     g = torch.Generator().manual_seed(cfg_seed)
     scale = hd ** -0.5 if scale is None else scale
@@ -40,7 +40,8 @@ def _block(cfg_seed, B, na, n_total, start, H, Hkv, hd, theta, qk_norm, window=N
                 n_total=n_total, q_work=q_work, out=out, n_head=H, n_head_kv=Hkv, head_dim=hd,
                 q_norm_w=None if wq is None else wq.cuda(),
                 k_norm_w=None if wk is None else wk.cuda(), rms_eps=1e-6,
-                out_f32=True, sliding_window=window, scale=scale, softcap=softcap)
+                out_f32=True, sliding_window=window, scale=scale, softcap=softcap,
+                precise=precise)
     dq, dk_in, dv_in = (x.to(torch.bfloat16).cuda() for x in (q, k, v))
     ca.attention_block_dev(dq, dk_in, dv_in, **args)
     torch.cuda.synchronize()
@@ -118,6 +119,10 @@ def test_c5_fullsize_rows(window, theta):
 def test_gemma_global_layer_head_dim_512_fullsize_rows():
     # c5's shape with the real DiffusionGemma global-layer heads: B4 S8192,
     # 16 query heads over 2 kv heads (GQA group 8), head_dim 512, QK-norm,
-    # soft-cap 50, scale 1.0 (forward.rs:341).
-    d = _block(6, 4, 8192, 8192, 0, 16, 2, 512, 1e6, True, softcap=50.0, scale=1.0)
+    # soft-cap 50, scale 1.0 (forward.rs:341). With scale 1.0 the normed
+    # scores reach the soft-cap and most rows are dominated by a few keys, so
+    # one bf16 rounding of the weights alone exceeds 2e-3: this runs the
+    # precise two-term weights, as the host drop-in does.
+    d = _block(6, 4, 8192, 8192, 0, 16, 2, 512, 1e6, True, softcap=50.0, scale=1.0,
+               precise=True)
     _check_rows(d, 2, 96, seed=11)
