@@ -475,7 +475,8 @@ def config_dict(args, cfg, world):
             "layers": len(cfg["layers"]),
             "l2": "flushed between steps (working set < 2x L2)" if flush
             else "inputs larger than L2, no flush",
-            "parallelism": f"dp{world} (independent sequences per rank)"}
+            "parallelism": f"dp{world} (independent sequences per rank)",
+            **({"only_layer": args.only_layer} if args.only_layer is not None else {})}
 
 
 def kernel_ms(wl, flush, scratch, reps):
@@ -520,19 +521,51 @@ def roofline(name, cfg, layers, ms, peaks, traffic_key=None):
 def run_head_sharded(args, cfg, world, rank, dev):
     """Head-sharded strong scaling of ONE global batch of the config: rank r
     computes kv heads [r * Hkv / N, (r + 1) * Hkv / N) and their query heads
-    of every sequence; per layer the batch runs in chunks of sequences, and
-    while chunk c+1 computes, chunk c's head slices are all-gathered (NCCL, on
-    a second stream) and placed into [tokens, n_head, head_dim] rows, the
-    layout o_proj consumes (src/model/forward.rs:345). Every rank generates
-    the same global inputs from one seed; rank 0 then recomputes the whole
-    batch on its own GPU and compares the gathered rows with it."""
+    of every sequence, and the head slices are reassembled into full
+    [tokens, n_head, head_dim] rows on every rank, the layout o_proj consumes
+    (src/model/forward.rs:345). Two forms are timed:
+
+    peer  the attention epilogue stores each finished tile into every rank's
+          receive buffer over NVLink (CUDA IPC mappings, canvas_attn.sharding.
+          PeerRows); one stream-ordered 4-byte all_reduce per step is the
+          barrier after which all rows are in place. This is `value`.
+    nccl  per layer and chunk of sequences, one NCCL all_gather_into_tensor
+          on a second stream overlapped with the next chunk's compute, then a
+          copy into head order.
+
+    Every rank generates the same global inputs from one seed; rank 0 then
+    recomputes the whole batch on its own GPU and compares both forms'
+    gathered rows with it."""
     import torch
     import torch.distributed as dist
-    from canvas_attn.sharding import head_shard
+    from canvas_attn.sharding import PeerRows, head_shard
     sh = head_shard(cfg["H"], cfg["Hkv"], world, rank)
     wl = Workload(cfg, dev, seed=4321, heads=(sh.q_begin, sh.q_end, sh.kv_begin, sh.kv_end))
     B, na, H, hd = cfg["B"], cfg["na"], cfg["H"], cfg["hd"]
     lh = wl.H
+    tok = B * na
+    ca = wl.ca
+
+    # --- peer form
+    recv = [PeerRows(tok, H, hd) for _ in wl.layers]
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step_peer(i):
+        import ctypes
+        for L, R in zip(wl.layers, recv):
+            out, peers, ors = R.slice_args(sh)
+            a = wl.block_args(L, i % wl.n_sets)
+            a.out = out.data_ptr()
+            a.out_row_stride = ors
+            arr = (ctypes.c_void_p * len(peers))(*peers)
+            a.peer_out = ctypes.cast(arr, ctypes.c_void_p)
+            a.n_peer_out = len(peers)
+            rc = ca.lib.ca_attention_block_dev(ctypes.byref(a), wl.stream.cuda_stream)
+            if rc != 0:
+                raise ca.CaError(rc, "ca_attention_block_dev (peer rows)")
+        dist.all_reduce(flag)  # every rank's stores are in place after this
+
+    # --- NCCL form
     n_chunks = max(1, min(args.hs_chunks, B))
     while B % n_chunks:
         n_chunks -= 1
@@ -540,10 +573,10 @@ def run_head_sharded(args, cfg, world, rank, dev):
     tok_c = bc * na
     comm = torch.cuda.Stream(dev)
     stage = torch.empty((n_chunks, world, tok_c, lh, hd), dtype=torch.bfloat16, device=dev)
-    full = [torch.empty((B * na, H, hd), dtype=torch.bfloat16, device=dev) for _ in wl.layers]
+    full = [torch.empty((tok, H, hd), dtype=torch.bfloat16, device=dev) for _ in wl.layers]
     done = [torch.cuda.Event() for _ in range(n_chunks)]
 
-    def step(i, gather=True):
+    def step_nccl(i, gather=True):
         for li, L in enumerate(wl.layers):
             for c in range(n_chunks):
                 wl.block(L, i, c * bc, (c + 1) * bc)
@@ -554,7 +587,7 @@ def run_head_sharded(args, cfg, world, rank, dev):
                 with torch.cuda.stream(comm):
                     src = L["out"][c * bc:(c + 1) * bc].view(-1)
                     dist.all_gather_into_tensor(stage[c].view(-1), src)
-                    # [world, tok_c, lh, hd] -> rows tok of [tokens, H, hd]
+                    # [world, tok_c, lh, hd] -> rows of [tokens, H, hd]
                     full[li][c * tok_c:(c + 1) * tok_c].view(tok_c, world, lh, hd).copy_(
                         stage[c].permute(1, 0, 2, 3))
         if gather:
@@ -562,9 +595,9 @@ def run_head_sharded(args, cfg, world, rank, dev):
             fin.record(comm)
             wl.stream.wait_event(fin)
 
-    def timed(gather):
+    def timed(fn):
         for i in range(args.warmup):
-            step(i, gather)
+            fn(i)
         torch.cuda.synchronize()
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
@@ -572,43 +605,74 @@ def run_head_sharded(args, cfg, world, rank, dev):
         torch.cuda.synchronize()
         for i in range(args.steps):
             ev[i][0].record(wl.stream)
-            step(i, gather)
+            fn(i)
             ev[i][1].record(wl.stream)
         torch.cuda.synchronize()
         barrier(world)
         return max_over_ranks(sum(a.elapsed_time(b) for a, b in ev), world)
 
-    comp = timed(False)
-    tot = timed(True)
+    comp = timed(lambda i: step_nccl(i, gather=False))
+    t_peer = timed(step_peer)
+    t_nccl = timed(step_nccl)
+    status = ca.device_status(wl.stream.cuda_stream)
+    assert status == 0, f"device-side status {status}"
+
+    # NCCL all-gather of the whole output payload alone (bus bandwidth).
+    payload = torch.empty(tok * lh * hd, dtype=torch.bfloat16, device=dev)
+    gbuf = torch.empty(world * payload.numel(), dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        dist.all_gather_into_tensor(gbuf, payload)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        dist.all_gather_into_tensor(gbuf, payload)
+    e1.record()
+    torch.cuda.synchronize()
+    ag_ms = max_over_ranks(e0.elapsed_time(e1) / 10, world)
+    ag_bytes = gbuf.numel() * 2
+    del payload, gbuf
+
     last = (args.steps - 1) % wl.n_sets
-    # Parity: rank 0 recomputes the whole global batch (all heads) on its own
-    # GPU from the same inputs and compares with the gathered rows.
     parity = None
     if rank == 0:
         ref = Workload(cfg, dev, seed=4321)
         for L in ref.layers:
             ref.block(L, last)
         torch.cuda.synchronize()
-        worst, exact = 0.0, True
-        for li, L in enumerate(ref.layers):
-            want = L["out"].view(B * na, H, hd)
-            exact = exact and torch.equal(full[li], want)
-            worst = max(worst, (full[li].float() - want.float()).abs().max().item())
-        parity = dict(max_abs_diff=worst, bit_identical=exact, rows_checked=B * na * H,
+        res = {}
+        for form, bufs in (("peer", [R.buf for R in recv]), ("nccl", full)):
+            worst, exact = 0.0, True
+            for li, L in enumerate(ref.layers):
+                want = L["out"].view(tok, H, hd)
+                exact = exact and torch.equal(bufs[li], want)
+                worst = max(worst, (bufs[li].float() - want.float()).abs().max().item())
+            res[form] = dict(max_abs_diff=worst, bit_identical=exact)
+        parity = dict(res, rows_checked=tok * H,
                       against="all heads of the same global batch run on one GPU")
         del ref
         torch.cuda.synchronize()
+    barrier(world)
+    for R in recv:
+        R.close()
     flops = step_flops(cfg) * args.steps
-    return dict(value=round(flops / (tot * 1e-3) / 1e12, 2), unit="TFLOP/s",
-                compute_only=round(flops / (comp * 1e-3) / 1e12, 2),
-                ms_per_step=round(tot / args.steps, 4),
+    tf = lambda ms: round(flops / (ms * 1e-3) / 1e12, 2)  # noqa: E731
+    return dict(value=tf(t_peer), unit="TFLOP/s", compute_only=tf(comp),
+                ms_per_step=round(t_peer / args.steps, 4),
                 compute_ms_per_step=round(comp / args.steps, 4),
+                gather="attention epilogue stores its tiles into every rank's receive "
+                       "buffer over NVLink (CUDA IPC peer mappings); one 4-byte all_reduce "
+                       "per step as the barrier",
+                nccl=dict(value=tf(t_nccl), ms_per_step=round(t_nccl / args.steps, 4),
+                          chunks=n_chunks,
+                          collective="per layer and chunk of sequences, one NCCL "
+                                     "all_gather_into_tensor on a second stream, then a "
+                                     "copy into head order"),
+                nccl_allgather_alone=dict(bytes_out=ag_bytes, ms=round(ag_ms, 4),
+                                          busbw_gbs=round(ag_bytes * (world - 1) / world
+                                                          / (ag_ms * 1e-3) / 1e9, 1)),
                 heads_per_rank=lh, kv_heads_per_rank=wl.Hkv,
-                global_batch=B, scaling="strong", chunks=n_chunks,
-                collective=("per layer and chunk of sequences, one NCCL "
-                            "all_gather_into_tensor on a second stream, overlapped "
-                            "with the next chunk's compute"),
-                parity=parity)
+                global_batch=B, scaling="strong", parity=parity)
 
 
 def run_ours(args, cfg):
@@ -807,12 +871,16 @@ def main():
                     help="skip the head-sharded (all-gather) leg under torchrun")
     ap.add_argument("--no-by-config", action="store_true",
                     help="skip the kernel-alone rooflines of the other configs")
+    ap.add_argument("--only-layer", type=int, default=None,
+                    help="time only this layer of the config (e.g. c5: 0 sliding, 5 global)")
     ap.add_argument("--hs-chunks", type=int, default=4,
                     help="chunks of sequences the head-sharded leg pipelines")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     cfg = CONFIGS[args.config]
+    if args.only_layer is not None:  # one layer of a multi-layer config (profiling)
+        cfg = dict(cfg, layers=[cfg["layers"][args.only_layer]])
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -40,6 +40,9 @@ EXPORTED_SYMBOLS = (
     "ca_attention_block_dev",
     "ca_attention_block_dev_noalloc",
     "ca_build_rope_table",
+    "ca_ipc_export",
+    "ca_ipc_import",
+    "ca_ipc_close",
     "ca_device_status",
     "ca_selftest_wait_timeout",
     "ca_selftest_wait_timeout_status",
@@ -80,7 +83,8 @@ class CaDevArgs(ctypes.Structure):
                 ("k_seq", ctypes.c_void_p), ("q_prefix", ctypes.c_void_p),
                 ("sliding_window", ctypes.c_int64), ("causal_prefix", ctypes.c_int64),
                 ("scale", ctypes.c_float), ("softcap", ctypes.c_float),
-                ("precise", ctypes.c_int32), ("status", ctypes.c_void_p)]
+                ("precise", ctypes.c_int32), ("status", ctypes.c_void_p),
+                ("peer_out", ctypes.c_void_p), ("n_peer_out", ctypes.c_int32)]
 
 
 class CaBlockArgs(ctypes.Structure):
@@ -97,7 +101,8 @@ class CaBlockArgs(ctypes.Structure):
                 ("head_dim", ctypes.c_int32), ("sliding_window", ctypes.c_int64),
                 ("causal_prefix", ctypes.c_int64), ("scale", ctypes.c_float),
                 ("softcap", ctypes.c_float), ("precise", ctypes.c_int32),
-                ("status", ctypes.c_void_p)]
+                ("status", ctypes.c_void_p), ("out_row_stride", ctypes.c_int64),
+                ("peer_out", ctypes.c_void_p), ("n_peer_out", ctypes.c_int32)]
 
 
 def _load():
@@ -125,6 +130,14 @@ def _load():
     L.ca_selftest_wait_timeout_status.argtypes = [ctypes.c_int64, ctypes.c_void_p,
                                                   ctypes.c_void_p]
     L.ca_selftest_wait_timeout_status.restype = ctypes.c_int
+    L.ca_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p,
+                                ctypes.POINTER(ctypes.c_uint64)]
+    L.ca_ipc_export.restype = ctypes.c_int
+    L.ca_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_uint64,
+                                ctypes.POINTER(ctypes.c_void_p)]
+    L.ca_ipc_import.restype = ctypes.c_int
+    L.ca_ipc_close.argtypes = [ctypes.c_void_p]
+    L.ca_ipc_close.restype = ctypes.c_int
     L.ca_status_string.argtypes = [ctypes.c_int]
     L.ca_status_string.restype = ctypes.c_char_p
     L.ca_version.restype = ctypes.c_char_p
@@ -224,6 +237,39 @@ def _ptr(x) -> Optional[int]:
     return int(x.data_ptr())
 
 
+def _peer_array(peer_out):
+    """peer_out: device pointers (ints or tensors) of other GPUs' buffers ->
+    (ctypes array or None, count)."""
+    if not peer_out:
+        return None, 0
+    ptrs = [_ptr(x) for x in peer_out]
+    return (ctypes.c_void_p * len(ptrs))(*ptrs), len(ptrs)
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_export(x):
+    """(handle bytes, byte offset) of device buffer x within its allocation,
+    for another process's ipc_import."""
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = ctypes.c_uint64(0)
+    _check(lib.ca_ipc_export(_ptr(x), h, ctypes.byref(off)), "ca_ipc_export")
+    return bytes(h.raw), int(off.value)
+
+
+def ipc_import(handle: bytes, offset: int) -> int:
+    """Maps another process's buffer (ipc_export's output) on the current
+    device; returns its device address (an int)."""
+    p = ctypes.c_void_p()
+    _check(lib.ca_ipc_import(handle, int(offset), ctypes.byref(p)), "ca_ipc_import")
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib.ca_ipc_close(int(ptr)), "ca_ipc_close")
+
+
 def _stream(stream) -> Optional[int]:
     if stream is None:
         return None
@@ -237,15 +283,19 @@ def make_dev_args(q, k, v, out, *, batch, sq, sk, n_head, n_head_kv, head_dim,
                   q_pos=None, k_pos=None, q_seq=None, k_seq=None, q_prefix=None,
                   sliding_window=None, causal_prefix=None, scale=1.0, softcap=0.0,
                   q_row_stride=0, kv_row_stride=0, out_row_stride=0,
-                  precise=False, status=None) -> CaDevArgs:
-    return CaDevArgs(_ptr(q), _ptr(k), _ptr(v), _ptr(out), 1 if out_f32 else 0,
+                  precise=False, status=None, peer_out=None) -> CaDevArgs:
+    peers, n_peers = _peer_array(peer_out)
+    a = CaDevArgs(_ptr(q), _ptr(k), _ptr(v), _ptr(out), 1 if out_f32 else 0,
                      q_row_stride, kv_row_stride, out_row_stride, batch, sq, sk,
                      _ptr(cu_q), _ptr(cu_k), max_sq, total_q, total_k,
                      n_head, n_head_kv, head_dim, _ptr(q_pos), _ptr(k_pos), _ptr(q_seq),
                      _ptr(k_seq), _ptr(q_prefix),
                      -1 if sliding_window is None else int(sliding_window),
                      -1 if causal_prefix is None else int(causal_prefix),
-                     float(scale), float(softcap), 1 if precise else 0, _ptr(status))
+                     float(scale), float(softcap), 1 if precise else 0, _ptr(status),
+                     ctypes.cast(peers, ctypes.c_void_p) if peers is not None else None, n_peers)
+    a._keep = peers
+    return a
 
 
 def attention_dev(q, k, v, out, *, stream=None, **kw) -> None:
@@ -262,14 +312,20 @@ def make_block_args(q, k, v, *, batch, n_active, active_pos, rope, rope_len, rop
                     cache_k, cache_v, n_total, q_work, out, n_head, n_head_kv, head_dim,
                     q_norm_w=None, k_norm_w=None, v_norm=False, rms_eps=1e-6,
                     out_f32=False, sliding_window=None, causal_prefix=None, scale=1.0,
-                    softcap=0.0, precise=False, status=None) -> CaBlockArgs:
-    return CaBlockArgs(_ptr(q), _ptr(k), _ptr(v), batch, n_active, _ptr(active_pos),
+                    softcap=0.0, precise=False, status=None, out_row_stride=0,
+                    peer_out=None) -> CaBlockArgs:
+    peers, n_peers = _peer_array(peer_out)
+    a = CaBlockArgs(_ptr(q), _ptr(k), _ptr(v), batch, n_active, _ptr(active_pos),
                        _ptr(q_norm_w), _ptr(k_norm_w), 1 if v_norm else 0, float(rms_eps),
                        _ptr(rope), rope_len, rope_dim, _ptr(cache_k), _ptr(cache_v), n_total,
                        _ptr(q_work), _ptr(out), 1 if out_f32 else 0, n_head, n_head_kv,
                        head_dim, -1 if sliding_window is None else int(sliding_window),
                        -1 if causal_prefix is None else int(causal_prefix), float(scale),
-                       float(softcap), 1 if precise else 0, _ptr(status))
+                       float(softcap), 1 if precise else 0, _ptr(status), int(out_row_stride),
+                       ctypes.cast(peers, ctypes.c_void_p) if peers is not None else None,
+                       n_peers)
+    a._keep = peers
+    return a
 
 
 def attention_block_dev(*args, stream=None, **kw) -> None:

@@ -68,3 +68,52 @@ def gather_heads(local_out, group=None):
     buf = torch.empty((world, tokens, lh, hd), dtype=local_out.dtype, device=local_out.device)
     dist.all_gather_into_tensor(buf.view(-1), local_out.contiguous().view(-1), group=group)
     return buf.permute(1, 0, 2, 3).reshape(tokens, world * lh, hd)
+
+
+class PeerRows:
+    """Receive buffers of a head-sharded layer, written directly by every rank.
+
+    Each rank allocates one [tokens, n_head, head_dim] buffer and exports it;
+    the others map it (CUDA IPC over NVLink). A rank then runs its attention
+    with `out` = its own head slice of its buffer (out_row_stride = n_head *
+    head_dim) and `peer_out` = the same slice of every other rank's buffer:
+    the attention epilogue stores each finished tile into all of them, so
+    after a barrier every rank holds the full rows o_proj consumes
+    (src/model/forward.rs:345), with no all-gather and no permute afterwards.
+
+    slice_args(shard) gives (out tensor view, peer pointers, out_row_stride)
+    for that rank's head range. Peers may overwrite a buffer on the next call,
+    so its owner must consume it before the ranks pass the next barrier.
+    """
+
+    def __init__(self, tokens: int, n_head: int, head_dim: int, dtype=None, group=None):
+        import torch
+        import torch.distributed as dist
+        import canvas_attn as ca
+        self._ca = ca
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        dtype = dtype or torch.bfloat16
+        self.buf = torch.empty((tokens, n_head, head_dim), dtype=dtype, device="cuda")
+        self.n_head, self.head_dim = n_head, head_dim
+        mine = ca.ipc_export(self.buf)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine, group=group)
+        base = self.buf.data_ptr()
+        self.peers = []  # (rank, mapped base address of that rank's buffer)
+        for r, (h, off) in enumerate(handles):
+            if r != self.rank:
+                self.peers.append((r, ca.ipc_import(h, off)))
+        self._base = base
+
+    def slice_args(self, shard: HeadShard):
+        """Output view and peer addresses of query heads [q_begin, q_end)."""
+        esz = self.buf.element_size()
+        off = shard.q_begin * self.head_dim * esz
+        out = self.buf[:, shard.q_begin:shard.q_end]
+        return out, [p + off for _, p in self.peers], self.n_head * self.head_dim
+
+    def close(self):
+        for _, p in self.peers:
+            self._ca.ipc_close(p)
+        self.peers = []

@@ -39,6 +39,7 @@ namespace ca {
 
 constexpr int kNoWindow = INT_MAX;
 
+constexpr int kMaxPeers = 7;  // other GPUs of one 8-GPU box
 constexpr int kFwdThreads = 352;  // 3 control warps + 8 softmax warps
 
 struct FwdParams {
@@ -73,6 +74,12 @@ struct FwdParams {
   int any_mask;       // any of: seq ids, prefixes, window, causal prefix (positions
                       // alone mask nothing: they matter only to those masks)
   int* err;           // device status word of this launch (null: g_device_error)
+  // Other GPUs' output buffers mapped into this process (same layout and
+  // strides as `out`): the epilogue stores every output row there as well,
+  // over NVLink, so a head-sharded layer's rows reach each rank's full
+  // [tokens, n_head, head_dim] buffer as the tiles finish.
+  void* peer_out[kMaxPeers];
+  int n_peer;
 };
 
 // Softmax organisation of a CTA (see the file comment):
@@ -488,6 +495,16 @@ __device__ __forceinline__ void fuse_q_prep(const FwdParams& p, uint32_t sQ, uin
   fence_proxy_async_smem();
   named_bar_sync(3, 256);
   if (tt == 0) mbar_arrive(bar_qr);
+}
+
+// Stores one 16-byte unit of an output row at element offset `off` of every
+// peer buffer (plain st.global over NVLink; peers are never read here).
+__device__ __forceinline__ void store_peers(const FwdParams& p, int64_t off, uint4 w) {
+#pragma unroll 1
+  for (int i = 0; i < p.n_peer; ++i) {
+    char* base = static_cast<char*>(p.peer_out[i]);
+    *reinterpret_cast<uint4*>(base + off * (p.out_f32 ? 4 : 2)) = w;
+  }
 }
 
 template <class C>
@@ -1146,6 +1163,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // by r & 7 (the tensor map's 128-byte swizzle); rows past the
         // sequence end and columns past head_dim are clipped by the store.
         uint8_t* stg = smem + C::kOffStage;
+        const int64_t obase = static_cast<int64_t>(gq) * p.out_row_stride +
+                              static_cast<int64_t>(head) * p.hd + ocol;
+        const bool to_peers = p.n_peer > 0 && row_valid;
         if (p.out_f32) {
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
@@ -1158,6 +1178,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             w.w = have ? v[u * 4 + 3] * inv : inv;
             *reinterpret_cast<float4*>(stg + ci * C::kStageChunk + r * 128 +
                                        ((uu ^ (r & 7)) << 4)) = w;
+            if (to_peers && ocol + col < p.hd)
+              store_peers(p, obase + col, *reinterpret_cast<const uint4*>(&w));
           }
         } else {
 #pragma unroll
@@ -1174,6 +1196,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             w.w = pack_bf16(w8[6], w8[7]);
             *reinterpret_cast<uint4*>(stg + ci * C::kStageChunk + r * 128 +
                                       ((uu ^ (r & 7)) << 4)) = w;
+            if (to_peers && ocol + col < p.hd) store_peers(p, obase + col, w);
           }
         }
       } else if (row_valid) {
@@ -1188,8 +1211,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             for (int i = 0; i < 8; ++i) w8[i] = have ? v[g8 * 8 + i] * inv : inv;
             if (p.out_f32) {
               float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase + col);
-              dst[0] = make_float4(w8[0], w8[1], w8[2], w8[3]);
-              dst[1] = make_float4(w8[4], w8[5], w8[6], w8[7]);
+              const float4 a = make_float4(w8[0], w8[1], w8[2], w8[3]);
+              const float4 b4 = make_float4(w8[4], w8[5], w8[6], w8[7]);
+              dst[0] = a;
+              dst[1] = b4;
+              if (p.n_peer) {
+                store_peers(p, obase + col, *reinterpret_cast<const uint4*>(&a));
+                store_peers(p, obase + col + 4, *reinterpret_cast<const uint4*>(&b4));
+              }
             } else {
               uint4 w;
               w.x = pack_bf16(w8[0], w8[1]);
@@ -1197,6 +1226,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               w.z = pack_bf16(w8[4], w8[5]);
               w.w = pack_bf16(w8[6], w8[7]);
               *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + obase + col) = w;
+              if (p.n_peer) store_peers(p, obase + col, w);
             }
           }
         }
@@ -1217,6 +1247,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   }
 
+  // Peer stores are performed at system scope before the kernel ends.
+  if (p.n_peer > 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

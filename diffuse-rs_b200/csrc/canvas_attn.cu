@@ -220,6 +220,13 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
                    : 0;
 
   p.err = a->status;
+  if (a->n_peer_out < 0 || a->n_peer_out > kMaxPeers || (a->n_peer_out > 0 && !a->peer_out))
+    return CA_ERR_INVALID;
+  p.n_peer = a->n_peer_out;
+  for (int i = 0; i < p.n_peer; ++i) {
+    if (!a->peer_out[i] || !aligned16(a->peer_out[i])) return CA_ERR_INVALID;
+    p.peer_out[i] = a->peer_out[i];
+  }
   p.fuse_q = fq != nullptr;
   p.fq_w = fq ? fq->w : nullptr;
   p.fq_rope = fq ? fq->rope : nullptr;
@@ -352,6 +359,9 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   d.v = a->cache_v;
   d.out = a->out;
   d.out_f32 = a->out_f32;
+  d.out_row_stride = a->out_row_stride;
+  d.peer_out = a->peer_out;
+  d.n_peer_out = a->n_peer_out;
   d.batch = a->batch;
   d.sq = a->n_active;
   d.sk = a->n_total;
@@ -714,7 +724,84 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns, int* status) {
 }  // namespace
 }  // namespace ca
 
+namespace ca {
+namespace {
+
+typedef CUresult (*AddrRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddrRangeFn addr_range_fn() {
+  static AddrRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddrRangeFn>(p);
+  });
+  return fn;
+}
+
+// Pointers ca_ipc_import returned -> the mapped allocation base to close.
+std::mutex g_ipc_mu;
+std::vector<std::pair<void*, void*>> g_ipc_maps;
+
+}  // namespace
+}  // namespace ca
+
 extern "C" {
+
+int ca_ipc_export(const void* dev_ptr, void* handle, uint64_t* offset) {
+  static_assert(sizeof(cudaIpcMemHandle_t) <= CA_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!dev_ptr || !handle || !offset) return CA_ERR_INVALID;
+  ca::AddrRangeFn fn = ca::addr_range_fn();
+  if (!fn) return CA_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return CA_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) {
+    cudaGetLastError();
+    return CA_ERR_CUDA;
+  }
+  std::memset(handle, 0, CA_IPC_HANDLE_BYTES);
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<uint64_t>(dev_ptr) - static_cast<uint64_t>(base);
+  return CA_OK;
+}
+
+int ca_ipc_import(const void* handle, uint64_t offset, void** dev_ptr) {
+  if (!handle || !dev_ptr) return CA_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return CA_ERR_CUDA;
+  }
+  void* p = static_cast<char*>(base) + offset;
+  std::lock_guard<std::mutex> lock(ca::g_ipc_mu);
+  ca::g_ipc_maps.emplace_back(p, base);
+  *dev_ptr = p;
+  return CA_OK;
+}
+
+int ca_ipc_close(void* dev_ptr) {
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(ca::g_ipc_mu);
+    for (size_t i = 0; i < ca::g_ipc_maps.size(); ++i)
+      if (ca::g_ipc_maps[i].first == dev_ptr) {
+        base = ca::g_ipc_maps[i].second;
+        ca::g_ipc_maps.erase(ca::g_ipc_maps.begin() + i);
+        break;
+      }
+  }
+  if (!base) return CA_ERR_INVALID;
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? CA_OK : CA_ERR_CUDA;
+}
 
 int ca_selftest_wait_timeout(int64_t limit_ns, void* stream) {
   if (limit_ns <= 0 || limit_ns > 1000000000ll) return CA_ERR_INVALID;

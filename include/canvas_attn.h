@@ -119,7 +119,14 @@ typedef struct {
                                 call's kernels is stored here (CA_ERR_TIMEOUT) instead
                                 of in the device-wide word that ca_device_status reads;
                                 the caller zeroes and reads it. NULL = device-wide word */
+    void* const* peer_out;   /* optional host array of n_peer_out device pointers into
+                                other GPUs' buffers mapped into this process (e.g. by
+                                ca_ipc_import): each receives exactly the rows written
+                                to `out`, at the same element offsets and strides, as
+                                the tiles finish (NVLink stores from the epilogue) */
+    int32_t n_peer_out;      /* 0 .. CA_MAX_PEERS */
 } ca_dev_args;
+#define CA_MAX_PEERS 7
 
 /*
  * ca_attention_dev -- the device-resident form of attention()
@@ -163,6 +170,10 @@ typedef struct {
     float softcap;
     int32_t precise;           /* as ca_dev_args.precise */
     int32_t* status;           /* as ca_dev_args.status */
+    int64_t out_row_stride;    /* elements between tokens of out; 0 = n_head * head_dim
+                                  (a head slice of a wider [tokens, heads, head_dim] buffer) */
+    void* const* peer_out;     /* as ca_dev_args.peer_out (same offsets as out) */
+    int32_t n_peer_out;
 } ca_block_args;
 
 /*
@@ -204,6 +215,25 @@ int ca_attention_block_dev(const ca_block_args* a, void* stream);
  */
 int ca_attention_block_dev_noalloc(const ca_block_args* a, void* stream);
 #define CA_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/*
+ * Peer buffers for head-sharded layers (no counterpart in the reference,
+ * whose CPU path has one address space). One process per GPU: a rank
+ * exports its receive buffer, the others import it and pass the mapping in
+ * peer_out, so the attention epilogue stores its head slice straight into
+ * every rank's [tokens, n_head, head_dim] buffer over NVLink.
+ * ca_ipc_export: handle (CA_IPC_HANDLE_BYTES bytes, opaque) and byte offset
+ * of dev_ptr within its allocation. ca_ipc_import: maps that allocation of
+ * another process on the current device and returns base + offset.
+ * ca_ipc_close: unmaps a pointer ca_ipc_import returned. A receive buffer may
+ * be rewritten by peers only after its owner has consumed it; the library
+ * does not order one call's peer stores against another's reads (use a
+ * barrier, e.g. a stream-ordered collective, between them).
+ */
+#define CA_IPC_HANDLE_BYTES 64
+int ca_ipc_export(const void* dev_ptr, void* handle, uint64_t* offset);
+int ca_ipc_import(const void* handle, uint64_t offset, void** dev_ptr);
+int ca_ipc_close(void* dev_ptr);
 
 /*
  * ca_build_rope_table -- replaces build_rope_cache_ff (src/model/ops.rs:398-416),

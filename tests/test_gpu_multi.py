@@ -1,10 +1,14 @@
-"""Head sharding across two GPUs with NCCL (skipped with fewer than 2 GPUs).
+"""Head sharding across two GPUs (skipped with fewer than 2 GPUs).
 
 Each rank runs the fused attention block on its own kv heads (and their
-query heads) of the same seeded batch, then one NCCL all-gather reassembles
-[tokens, n_head, head_dim] rows, the layout o_proj consumes
-(src/model/forward.rs:345). A kv head's work does not depend on the other
-heads, so the gathered result must equal a single-GPU run bit for bit."""
+query heads) of the same seeded batch, and the head slices are reassembled
+into [tokens, n_head, head_dim] rows, the layout o_proj consumes
+(src/model/forward.rs:345): once with an NCCL all-gather, once by the
+attention epilogue storing its tiles straight into both ranks' receive
+buffers over NVLink (CUDA IPC peer mappings). A kv head's work does not
+depend on the other heads, so both gathered results must equal a single-GPU
+run bit for bit. NVLS is off (NCCL_NVLS_ENABLE=0) and the peer stores are
+plain st.global, no multicast."""
 import os
 import socket
 
@@ -26,20 +30,22 @@ def _inputs():
     return q, k, v, wq, wk
 
 
-def _block(q, k, v, wq, wk, h, hkv, dev):
+def _block(q, k, v, wq, wk, h, hkv, dev, out=None, peer_out=None, out_row_stride=0):
     import canvas_attn as ca
     rope = torch.from_numpy(ca.build_rope_cache(4096, HD, 5e4)).to(dev)
     pos = torch.arange(S, dtype=torch.int32, device=dev).repeat(B, 1).contiguous()
     cache_k = torch.zeros(B, S, hkv, HD, dtype=torch.bfloat16, device=dev)
     cache_v = torch.zeros_like(cache_k)
     q_work = torch.empty(B, S, h, HD, dtype=torch.bfloat16, device=dev)
-    out = torch.empty(B, S, h, HD, dtype=torch.bfloat16, device=dev)
+    if out is None:
+        out = torch.empty(B, S, h, HD, dtype=torch.bfloat16, device=dev)
     ca.attention_block_dev(q.contiguous().to(dev), k.contiguous().to(dev),
                            v.contiguous().to(dev), batch=B, n_active=S, active_pos=pos,
                            rope=rope, rope_len=4096, rope_dim=HD, cache_k=cache_k,
                            cache_v=cache_v, n_total=S, q_work=q_work, out=out, n_head=h,
                            n_head_kv=hkv, head_dim=HD, q_norm_w=wq.to(dev), k_norm_w=wk.to(dev),
-                           rms_eps=1e-6, scale=HD ** -0.5)
+                           rms_eps=1e-6, scale=HD ** -0.5, peer_out=peer_out,
+                           out_row_stride=out_row_stride)
     return out
 
 
@@ -50,7 +56,7 @@ def _worker(rank, world, port, result_path):
     sys.path[:0] = [os.path.join(root, "diffuse-rs_b200"), root]
     import torch.distributed as dist
     import canvas_attn as ca
-    from canvas_attn.sharding import gather_heads, head_shard
+    from canvas_attn.sharding import PeerRows, gather_heads, head_shard
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -64,22 +70,32 @@ def _worker(rank, world, port, result_path):
                      v[:, :, sh.kv_begin:sh.kv_end], wq, wk, sh.q_end - sh.q_begin,
                      sh.kv_end - sh.kv_begin, dev)
         full = gather_heads(out.view(B * S, sh.q_end - sh.q_begin, HD))
+        # Peer form: the epilogue writes both ranks' receive buffers.
+        recv = PeerRows(B * S, H, HD)
+        pout, peers, ors = recv.slice_args(sh)
+        _block(q[:, :, sh.q_begin:sh.q_end], k[:, :, sh.kv_begin:sh.kv_end],
+               v[:, :, sh.kv_begin:sh.kv_end], wq, wk, sh.q_end - sh.q_begin,
+               sh.kv_end - sh.kv_begin, dev, out=pout, peer_out=peers, out_row_stride=ors)
         torch.cuda.synchronize()
+        dist.barrier()
         assert ca.device_status() == ca.CA_OK
         if rank == 0:
             ref = _block(q, k, v, wq, wk, H, HKV, dev).view(B * S, H, HD)
             torch.cuda.synchronize()
-            ok = torch.equal(full, ref)
-            diff = (full.float() - ref.float()).abs().max().item()
+            ok = torch.equal(full, ref) and torch.equal(recv.buf, ref)
+            diff = max((full.float() - ref.float()).abs().max().item(),
+                       (recv.buf.float() - ref.float()).abs().max().item())
             with open(result_path, "w") as f:
                 f.write(f"{int(ok)} {diff}\n")
+        dist.barrier()
+        recv.close()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
-def test_head_sharded_block_with_nccl_gather_matches_one_gpu(tmp_path):
+def test_head_sharded_block_gathers_match_one_gpu(tmp_path):
     import torch.multiprocessing as mp
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
