@@ -1247,8 +1247,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   }
 
-  // Peer stores are performed at system scope before the kernel ends.
-  if (p.n_peer > 0) __threadfence_system();
+  // Peer stores need no fence here: a CTA that waited for them would hold
+  // its SM idle, and the grid's completion already orders them before any
+  // stream-ordered barrier the host issues afterwards.
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
