@@ -611,7 +611,7 @@ def run_head_sharded(args, cfg, world, rank, dev):
         barrier(world)
         return max_over_ranks(sum(a.elapsed_time(b) for a, b in ev), world)
 
-    comp = timed(lambda i: step_nccl(i, gather=False))
+    comp = timed(wl.step)  # the peer form's launches (whole batch per layer), no gather
     t_peer = timed(step_peer)
     t_nccl = timed(step_nccl)
     status = ca.device_status(wl.stream.cuda_stream)
