@@ -57,6 +57,7 @@ struct FwdParams {
   const int* q_seq;
   const int* k_seq;
   const int* q_prefix;
+  const int* seq_prefix;  // per-sequence causal prefix [batch] (when q_prefix is null)
   int window;         // kNoWindow = None
   int causal_prefix;  // -1 = None
   float scale;
@@ -284,8 +285,9 @@ __device__ __forceinline__ void seq_range(const FwdParams& p, int b, int& q_beg,
 // visible) and compact the visible ones into `list` (kind in bits 14-15). The per-tile flags are first written in place into `list`
 // and then compacted; misc[1] receives the count.
 template <class C>
-__device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_beg, int k_len,
-                                int t0, int span, uint16_t* list, int* misc, int tid64) {
+__device__ void build_tile_list(const FwdParams& p, int b, int q_beg, int q_len, int k_beg,
+                                int k_len, int t0, int span, uint16_t* list, int* misc,
+                                int tid64) {
   uint16_t* flags = list;
   const int lane = tid64 & 31;
   const int w = tid64 >> 5;  // 0..1
@@ -310,7 +312,8 @@ __device__ void build_tile_list(const FwdParams& p, int q_beg, int q_len, int k_
       const int g = q_beg + tl;
       const int qp = p.q_pos ? p.q_pos[g] : tl;
       const int qsq = p.q_seq ? p.q_seq[g] : 0;
-      const int pre = p.q_prefix ? p.q_prefix[g] : p.causal_prefix;
+      const int pre = p.q_prefix ? p.q_prefix[g]
+                                 : p.seq_prefix ? p.seq_prefix[b] : p.causal_prefix;
       pmin = min(pmin, qp); pmax = max(pmax, qp);
       smin = min(smin, qsq); smax = max(smax, qsq);
       if (pre >= 0 && qp < pre) { cpmin = min(cpmin, qp); ++ncaus; }
@@ -497,8 +500,16 @@ __device__ __forceinline__ void fuse_q_prep(const FwdParams& p, uint32_t sQ, uin
   if (tt == 0) mbar_arrive(bar_qr);
 }
 
+// Output tensor maps of the peer buffers (same shape as tm_o), used when the
+// epilogue stores through TMA: the bulk copies to other GPUs run on the TMA
+// engine after the tile is staged, so the CTA does not wait on NVLink.
+struct PeerMaps {
+  CUtensorMap m[kMaxPeers];
+};
+
 // Stores one 16-byte unit of an output row at element offset `off` of every
-// peer buffer (plain st.global over NVLink; peers are never read here).
+// peer buffer (plain st.global over NVLink; peers are never read here). Used
+// by the row-store epilogue (variable-length batches).
 __device__ __forceinline__ void store_peers(const FwdParams& p, int64_t off, uint4 w) {
 #pragma unroll 1
   for (int i = 0; i < p.n_peer; ++i) {
@@ -512,7 +523,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
-                    const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
+                    const __grid_constant__ CUtensorMap tm_o, const FwdParams p,
+                    const __grid_constant__ PeerMaps pm) {
   constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST, STK = C::STK;
   constexpr bool ALT = C::ALT, SPLIT = C::SPLIT;
   // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
@@ -605,7 +617,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tmem_relinquish();
   }
   if (warp <= 1)
-    build_tile_list<C>(p, q_beg, q_len, k_beg, k_len, t0, p.QT, list, misc, tid);
+    build_tile_list<C>(p, b, q_beg, q_len, k_beg, k_len, t0, p.QT, list, misc, tid);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -752,7 +764,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (row_valid && p.any_mask) {
       qpos = p.q_pos ? p.q_pos[gq] : t_local;
       qseq = p.q_seq ? p.q_seq[gq] : 0;
-      qpre = p.q_prefix ? p.q_prefix[gq] : p.causal_prefix;
+      qpre = p.q_prefix ? p.q_prefix[gq] : p.seq_prefix ? p.seq_prefix[b] : p.causal_prefix;
     }
     const float sl2 = p.scale_log2;
     const bool fast_ok = p.softcap == 0.f && sl2 >= 0.f;
@@ -760,7 +772,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // visibility within a tile is a band test on the key index.
     // (window 0 makes every key invisible: left to the generic form.)
     const bool band_ok = p.window != kNoWindow && p.window > 0 && !p.k_pos && !p.k_seq &&
-                         !p.q_seq && !p.q_prefix && p.causal_prefix < 0;
+                         !p.q_seq && !p.q_prefix && !p.seq_prefix && p.causal_prefix < 0;
     // Soft-cap: logit = cap * tanh(score * scale / cap), in log2 units.
     const float scale_cap = p.softcap != 0.f ? p.scale / p.softcap : 0.f;
     const float cap_l2 = p.softcap * 1.4426950408889634f;
@@ -1163,9 +1175,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // by r & 7 (the tensor map's 128-byte swizzle); rows past the
         // sequence end and columns past head_dim are clipped by the store.
         uint8_t* stg = smem + C::kOffStage;
-        const int64_t obase = static_cast<int64_t>(gq) * p.out_row_stride +
-                              static_cast<int64_t>(head) * p.hd + ocol;
-        const bool to_peers = p.n_peer > 0 && row_valid;
         if (p.out_f32) {
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
@@ -1178,8 +1187,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             w.w = have ? v[u * 4 + 3] * inv : inv;
             *reinterpret_cast<float4*>(stg + ci * C::kStageChunk + r * 128 +
                                        ((uu ^ (r & 7)) << 4)) = w;
-            if (to_peers && ocol + col < p.hd)
-              store_peers(p, obase + col, *reinterpret_cast<const uint4*>(&w));
           }
         } else {
 #pragma unroll
@@ -1196,7 +1203,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             w.w = pack_bf16(w8[6], w8[7]);
             *reinterpret_cast<uint4*>(stg + ci * C::kStageChunk + r * 128 +
                                       ((uu ^ (r & 7)) << 4)) = w;
-            if (to_peers && ocol + col < p.hd) store_peers(p, obase + col, w);
           }
         }
       } else if (row_valid) {
@@ -1238,9 +1244,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       named_bar_sync(2, 256);
       if (warp == 3 && lane == 0) {
         const int inner = p.out_f32 ? 32 : 64;  // elements per 128-byte chunk
-        for (int ci = 0; ci * inner < C::HDO && ocol + ci * inner < p.hd; ++ci)
-          tma_store_4d(&tm_o, smem_u32(smem + C::kOffStage + ci * C::kStageChunk),
-                       ocol + ci * inner, kvh * p.G, t0, b);
+        for (int ci = 0; ci * inner < C::HDO && ocol + ci * inner < p.hd; ++ci) {
+          const uint32_t src = smem_u32(smem + C::kOffStage + ci * C::kStageChunk);
+          tma_store_4d(&tm_o, src, ocol + ci * inner, kvh * p.G, t0, b);
+          // The same tile into every peer's buffer (head-sharded layers).
+          for (int i = 0; i < p.n_peer; ++i)
+            tma_store_4d(&pm.m[i], src, ocol + ci * inner, kvh * p.G, t0, b);
+        }
         bulk_commit_group();
         bulk_wait_group_read0();
       }

@@ -118,6 +118,14 @@ struct Launch {
                       p->out_f32 != 0, p->G, p->QT) != CA_OK)
       pl.tma_out = 0;
     if (!pl.tma_out) to = tq;  // unused
+    // Peer buffers: tensor maps of the same shape for the TMA epilogue;
+    // the row-store epilogue writes them with plain stores instead.
+    PeerMaps pm;
+    std::memset(&pm, 0, sizeof(pm));
+    for (int i = 0; pl.tma_out && i < pl.n_peer; ++i)
+      if (make_tmap_out(&pm.m[i], pl.peer_out[i], hd, p->n_head, p->sq, p->batch,
+                        p->out_row_stride, p->out_f32 != 0, p->G, p->QT) != CA_OK)
+        return CA_ERR_INVALID;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
     if (!attr_done[dev]) {
@@ -128,7 +136,7 @@ struct Launch {
     }
     const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
     dim3 grid(n_qtiles * C::OS, p->n_head_kv, p->batch);
-    attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, to, pl);
+    attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, to, pl, pm);
     return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
   }
 };
@@ -204,6 +212,7 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
   p.q_seq = a->q_seq;
   p.k_seq = a->k_seq;
   p.q_prefix = a->q_prefix;
+  p.seq_prefix = a->seq_prefix;
   p.window = a->sliding_window < 0 ? kNoWindow
                                    : static_cast<int>(a->sliding_window >= INT_MAX
                                                           ? INT_MAX - 1
@@ -214,8 +223,8 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
   p.softcap = a->softcap > 0.f ? a->softcap : 0.f;
   // Positions alone mask nothing (visible() reads them only for the window
   // and the causal prefix), so they do not make a mask by themselves.
-  p.any_mask = (a->q_seq || a->k_seq || a->q_prefix || p.window != kNoWindow ||
-                p.causal_prefix >= 0)
+  p.any_mask = (a->q_seq || a->k_seq || a->q_prefix || a->seq_prefix ||
+                p.window != kNoWindow || p.causal_prefix >= 0)
                    ? 1
                    : 0;
 
@@ -274,7 +283,8 @@ namespace {
 // 16-byte aligned and rope_dim % 16 == 0.
 bool block_fuses_q(const ca_block_args* a, bool vec) {
   const int H = a->n_head, Hkv = a->n_head_kv;
-  if (!CA_FUSE_Q || !vec || a->head_dim != 128 || a->rope_dim != 128 || H / Hkv > 128)
+  if (!CA_FUSE_Q || !vec || a->head_dim != 128 || a->rope_dim != 128 || H / Hkv > 128 ||
+      a->cu_active)
     return false;
   const long long fq_ctas = static_cast<long long>(a->batch) * Hkv *
                             ((a->n_active + 128 / (H / Hkv) - 1) / (128 / (H / Hkv)));
@@ -293,12 +303,15 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
       !a->cache_v || !a->q_work || !a->out)
     return CA_ERR_INVALID;
   const int H = a->n_head, Hkv = a->n_head_kv, hd = a->head_dim;
-  if (a->batch < 0 || a->n_active < 0 || a->n_total < a->n_active || H <= 0 || Hkv <= 0 ||
-      hd <= 0 || H % Hkv)
+  const bool varlen = a->cu_active != nullptr;
+  if (a->batch < 0 || H <= 0 || Hkv <= 0 || hd <= 0 || H % Hkv) return CA_ERR_INVALID;
+  if (varlen ? (!a->cu_total || a->total_active < 0 || a->total_cache < 0 || a->max_active < 0)
+             : (a->n_active < 0 || a->n_total < a->n_active))
     return CA_ERR_INVALID;
   if (a->rope_dim < 0 || a->rope_dim > hd || a->rope_dim % 2 || a->rope_len <= 0)
     return CA_ERR_INVALID;
-  if (a->batch == 0 || a->n_active == 0) return CA_OK;
+  if (a->batch == 0 || (varlen ? a->total_active == 0 : a->n_active == 0)) return CA_OK;
+  if (varlen && (a->total_active > INT_MAX || a->total_cache > INT_MAX)) return CA_ERR_UNSUPPORTED;
   PrepParams pp{};
   pp.q = static_cast<const __nv_bfloat16*>(a->q);
   pp.k = static_cast<const __nv_bfloat16*>(a->k);
@@ -317,6 +330,9 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   pp.batch = a->batch;
   pp.na = a->n_active;
   pp.n_total = a->n_total;
+  pp.cu_active = a->cu_active;
+  pp.cu_total = a->cu_total;
+  pp.total_active = varlen ? a->total_active : 0;
   const bool vec = block_vec(a);
   // head_dim 128 with rotation over the whole head: the attention kernel
   // normalises and rotates its own Q tile (each Q row belongs to exactly one
@@ -331,9 +347,10 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   pp.H = Hp;
   pp.Hkv = Hkv;
   pp.hd = hd;
-  const long long jobs = static_cast<long long>(a->batch) * a->n_active * (Hp + 2 * Hkv);
+  const long long toks =
+      varlen ? a->total_active : static_cast<long long>(a->batch) * a->n_active;
+  const long long jobs = toks * (Hp + 2 * Hkv);
   if (vec && (hd == 64 || hd == 128 || hd == 256)) {
-    const long long toks = static_cast<long long>(a->batch) * a->n_active;
     // 16-row jobs unless that leaves fewer jobs than 64 warps per SM; then
     // one warp step per job (256 / head_dim rows).
     pp.rows_per_job = 16;
@@ -371,10 +388,18 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   d.q_pos = a->active_pos;  // keys are positions 0..n_total-1 in order: k_pos = identity
   d.sliding_window = a->sliding_window;
   d.causal_prefix = a->causal_prefix;
+  d.seq_prefix = a->seq_prefix;
   d.scale = a->scale;
   d.softcap = a->softcap;
   d.precise = a->precise;
   d.status = a->status;
+  if (varlen) {  // keys of sequence b: its cache rows, positions 0.. in order
+    d.cu_q = a->cu_active;
+    d.cu_k = a->cu_total;
+    d.total_q = a->total_active;
+    d.total_k = a->total_cache;
+    d.max_sq = a->max_active;
+  }
   if (fuse_q) {
     const QFuse fq{a->q_norm_w, a->rope, a->rms_eps};
     return attention_dev_impl(&d, st, &fq);
@@ -678,7 +703,8 @@ int noalloc_scratch(int dev, void** out) {
 int noalloc_impl(const ca_block_args* a, cudaStream_t st) {
   if (!a) return CA_ERR_INVALID;
   if (a->q_work) return CA_ERR_INVALID;  // the library supplies the scratch
-  if (a->batch < 0 || a->n_active < 0 || a->n_head <= 0 || a->n_head_kv <= 0 ||
+  if (a->batch < 0 || a->n_active < 0 || (a->cu_active && a->total_active < 0) ||
+      a->n_head <= 0 || a->n_head_kv <= 0 ||
       a->head_dim <= 0)
     return CA_ERR_INVALID;
   int dev = 0;
@@ -693,7 +719,8 @@ int noalloc_impl(const ca_block_args* a, cudaStream_t st) {
   // The size test divides step by step so that no product can wrap.
   if (!block_fuses_q(&b, block_vec(&b))) {
     unsigned long long room = kNoAllocElems;
-    const int64_t f[4] = {a->batch, a->n_active, a->n_head, a->head_dim};
+    const int64_t f[4] = {a->cu_active ? 1 : a->batch,
+                          a->cu_active ? a->total_active : a->n_active, a->n_head, a->head_dim};
     const bool empty = f[0] == 0 || f[1] == 0;
     for (int i = 0; i < 4 && !empty; ++i) {
       if (static_cast<unsigned long long>(f[i]) > room) return CA_ERR_SCRATCH;

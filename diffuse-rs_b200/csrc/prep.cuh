@@ -34,7 +34,30 @@ struct PrepParams {
   // the rows a warp covers per step): 16 for large batches; small batches
   // use one step per job so that more warps share the short pass.
   int rows_per_job;
+  // Variable-length batches (cu_active != null): sequence b owns active rows
+  // cu_active[b] .. cu_active[b+1]-1 and cache rows cu_total[b] ..; the
+  // cache row of a token is cu_total[b] + its position.
+  const int* cu_active;
+  const int* cu_total;
+  long long total_active;
 };
+
+// Active tokens of the whole call.
+__device__ __forceinline__ long long prep_tokens(const PrepParams& p) {
+  return p.cu_active ? p.total_active : static_cast<long long>(p.batch) * p.na;
+}
+
+// Cache row (sequence base + position) of active token `tok`.
+__device__ __forceinline__ long long cache_row(const PrepParams& p, long long tok, int pos) {
+  if (!p.cu_active) return static_cast<long long>(tok / p.na) * p.n_total + pos;
+  int lo = 0, hi = p.batch - 1;  // last b with cu_active[b] <= tok
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.cu_active + mid) <= tok) lo = mid;
+    else hi = mid - 1;
+  }
+  return static_cast<long long>(__ldg(p.cu_total + lo)) + pos;
+}
 
 __device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -56,13 +79,13 @@ __global__ void __launch_bounds__(256) prep_block_kernel(const PrepParams p) {
   float* buf = prep_smem + warp * p.hd;
   const int rows_q = p.H, rows_kv = p.Hkv;
   const int per_tok = rows_q + 2 * rows_kv;
-  const long long jobs = static_cast<long long>(p.batch) * p.na * per_tok;
+  const long long jobs = prep_tokens(p) * per_tok;
   for (long long job = static_cast<long long>(blockIdx.x) * 8 + warp; job < jobs;
        job += static_cast<long long>(gridDim.x) * 8) {
     const long long tok = job / per_tok;  // b * na + t
     const int r = static_cast<int>(job % per_tok);
-    const int b = static_cast<int>(tok / p.na);
     const int pos = p.pos[tok];
+    const long long crow = cache_row(p, tok, pos);
     const __nv_bfloat16* src;
     __nv_bfloat16* dst;
     const float* w = nullptr;
@@ -75,13 +98,13 @@ __global__ void __launch_bounds__(256) prep_block_kernel(const PrepParams p) {
     } else if (r < rows_q + rows_kv) {
       const int h = r - rows_q;
       src = p.k + (tok * p.Hkv + h) * p.hd;
-      dst = p.cache_k + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * p.hd;
+      dst = p.cache_k + (crow * p.Hkv + h) * p.hd;
       w = p.k_norm_w;
       norm = w != nullptr;
     } else {
       const int h = r - rows_q - rows_kv;
       src = p.v + (tok * p.Hkv + h) * p.hd;
-      dst = p.cache_v + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * p.hd;
+      dst = p.cache_v + (crow * p.Hkv + h) * p.hd;
       norm = p.v_norm != 0;
       rope = false;  // V is not rotated (forward.rs:310 rotates Q and K only)
     }
@@ -122,7 +145,7 @@ __global__ void __launch_bounds__(256) prep_token_kernel(const PrepParams p) {
   const int sub = lane / LPR, sl = lane % LPR;
   const int e0 = sl * 8;
   const int half = p.rope_dim / 2;
-  const long long n_tok = static_cast<long long>(p.batch) * p.na;
+  const long long n_tok = prep_tokens(p);
   const int per_tok = p.H + 2 * p.Hkv;
   // A job is up to rows_per_job rows of one token.
   const int kRowsPerJob = p.rows_per_job;
@@ -135,7 +158,7 @@ __global__ void __launch_bounds__(256) prep_token_kernel(const PrepParams p) {
     const int row_beg = static_cast<int>(job % chunks) * kRowsPerJob;
     const int row_end = min(per_tok, row_beg + kRowsPerJob);
     const int pos = __ldg(p.pos + tok);
-    const int b = static_cast<int>(tok / p.na);
+    const long long crow = cache_row(p, tok, pos);
     // This lane's 8 (sin, cos) pairs: entries e0..e0+7 of the lower or upper
     // half map to table entries (e0 mod half)..+7; rope_dim % 16 == 0 keeps
     // them inside one half.
@@ -169,13 +192,13 @@ __global__ void __launch_bounds__(256) prep_token_kernel(const PrepParams p) {
       } else if (rr < p.H + p.Hkv) {
         const int h = rr - p.H;
         src = p.k + (tok * p.Hkv + h) * HD;
-        dst = p.cache_k + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
+        dst = p.cache_k + (crow * p.Hkv + h) * HD;
         w = p.k_norm_w;
         norm = w != nullptr;
       } else {
         const int h = rr - p.H - p.Hkv;
         src = p.v + (tok * p.Hkv + h) * HD;
-        dst = p.cache_v + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
+        dst = p.cache_v + (crow * p.Hkv + h) * HD;
         norm = p.v_norm != 0;
         rope = false;  // V is not rotated (forward.rs:310 rotates Q and K only)
       }
@@ -280,7 +303,7 @@ __global__ void __launch_bounds__(256) prep_pair_kernel(const PrepParams p) {
       wk[4 + i] = __ldg(p.k_norm_w + HALF + e0 + i);
     }
   }
-  const long long n_tok = static_cast<long long>(p.batch) * p.na;
+  const long long n_tok = prep_tokens(p);
   const int per_tok = p.H + 2 * p.Hkv;
   const int chunks = (per_tok + kRowsPerJob - 1) / kRowsPerJob;
   const long long n_jobs = n_tok * chunks;
@@ -290,7 +313,7 @@ __global__ void __launch_bounds__(256) prep_pair_kernel(const PrepParams p) {
     const int row_beg = static_cast<int>(job % chunks) * kRowsPerJob;
     const int row_end = min(per_tok, row_beg + kRowsPerJob);
     const int pos = __ldg(p.pos + tok);
-    const int b = static_cast<int>(tok / p.na);
+    const long long crow = cache_row(p, tok, pos);
     float sn[4], cs[4];
     {
       const float4* t4 =
@@ -313,12 +336,12 @@ __global__ void __launch_bounds__(256) prep_pair_kernel(const PrepParams p) {
       } else if (rr < p.H + p.Hkv) {
         const int h = rr - p.H;
         src = p.k + (tok * p.Hkv + h) * HD;
-        dst = p.cache_k + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
+        dst = p.cache_k + (crow * p.Hkv + h) * HD;
         kind = 1;
       } else {
         const int h = rr - p.H - p.Hkv;
         src = p.v + (tok * p.Hkv + h) * HD;
-        dst = p.cache_v + ((static_cast<long long>(b) * p.n_total + pos) * p.Hkv + h) * HD;
+        dst = p.cache_v + (crow * p.Hkv + h) * HD;
         kind = 2;
       }
       const uint2 lo = __ldg(reinterpret_cast<const uint2*>(src + e0));

@@ -125,6 +125,10 @@ typedef struct {
                                 to `out`, at the same element offsets and strides, as
                                 the tiles finish (NVLink stores from the epilogue) */
     int32_t n_peer_out;      /* 0 .. CA_MAX_PEERS */
+    const int32_t* seq_prefix; /* optional int32 [batch]: causal prefix of each sequence
+                                  (Gemma's per-sequence canvas_start, forward.rs:153-160),
+                                  negative = None; used when q_prefix is NULL and
+                                  overrides causal_prefix */
 } ca_dev_args;
 #define CA_MAX_PEERS 7
 
@@ -174,6 +178,18 @@ typedef struct {
                                   (a head slice of a wider [tokens, heads, head_dim] buffer) */
     void* const* peer_out;     /* as ca_dev_args.peer_out (same offsets as out) */
     int32_t n_peer_out;
+    /* Variable-length batches (the block-diagonal rows of forward_batch,
+     * src/model/forward.rs:118-169): with cu_active set, sequence b's active
+     * rows are rows cu_active[b] .. cu_active[b+1]-1 of q/k/v/active_pos/out
+     * (n_active is ignored), and its cache is rows cu_total[b] ..
+     * cu_total[b+1]-1 of cache_k/cache_v, position p at row cu_total[b] + p;
+     * its keys are all of those positions. */
+    const int32_t* cu_active;  /* int32 [batch + 1] or NULL (uniform) */
+    const int32_t* cu_total;   /* int32 [batch + 1], required with cu_active */
+    int32_t max_active;        /* varlen: largest per-sequence active count */
+    int64_t total_active;      /* varlen: cu_active[batch] */
+    int64_t total_cache;       /* varlen: cu_total[batch] */
+    const int32_t* seq_prefix; /* as ca_dev_args.seq_prefix */
 } ca_block_args;
 
 /*

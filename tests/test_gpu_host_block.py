@@ -294,3 +294,61 @@ def test_block_pre_ops_variants(hd, rope_dim, v_norm, qk_norm, unaligned, S):
                                    atol=1e-2, rtol=1e-2, err_msg=what)
         ref = oracle_attention(qq, kk, vv, nq=S, nk=S, h=H, hkv=Hkv, hd=hd, scale=hd ** -0.5)
         check_close(got[b], ref, H, hd, what=f"{what} b={b}")
+
+
+@pytest.mark.parametrize("hd,qk_norm,v_norm,gemma", [
+    (128, True, False, False),   # LLaDA-style: QK-norm, 1/sqrt(d), no prefix
+    (256, True, True, True),     # Gemma-style: V norm, scale 1.0, per-sequence causal prompt
+    (512, True, True, True),     # Gemma global layer heads
+])
+def test_block_varlen_block_diagonal_batch(hd, qk_norm, v_norm, gemma):
+    """forward_batch (src/model/forward.rs:118-169) through the fused block:
+    ragged sequences concatenated row-wise, each row with its own position,
+    keys = its own sequence only, Gemma's causal prompt up to each sequence's
+    own canvas_start. Checked against the reference's block-diagonal call
+    (seq ids + per-row prefix over the concatenated rows)."""
+    lens = [150, 1, 300, 77]
+    starts = [40, 0, 120, 77]  # canvas_start per sequence (Gemma's causal prompt)
+    B, H, Hkv = len(lens), 8, 2
+    eps, theta = 1e-6, 10000.0
+    scale = 1.0 if gemma else hd ** -0.5
+    g = torch.Generator().manual_seed(hd + 3)
+    n = sum(lens)
+    q = bf16_round(randn(g, n, H, hd))
+    k = bf16_round(randn(g, n, Hkv, hd))
+    v = bf16_round(randn(g, n, Hkv, hd))
+    wq = torch.rand(hd, generator=g) + 0.5 if qk_norm else None
+    wk = torch.rand(hd, generator=g) + 0.5 if qk_norm else None
+    if gemma:  # keep scale-1.0 scores moderate
+        wq = wq * 0.1
+    rope = ca.build_rope_cache(4096, hd, theta)
+    pos = np.concatenate([np.arange(m) for m in lens])
+    seq = np.concatenate([np.full(m, i) for i, m in enumerate(lens)])
+    cu = torch.tensor(np.cumsum([0] + lens), dtype=torch.int32, device="cuda")
+    cache_k = torch.zeros(n, Hkv, hd, dtype=torch.bfloat16, device="cuda")
+    cache_v = torch.zeros_like(cache_k)
+    q_work = torch.empty(n, H, hd, dtype=torch.bfloat16, device="cuda")
+    out = torch.full((n, H, hd), float("inf"), device="cuda")
+    prefix_d = torch.tensor(starts, dtype=torch.int32, device="cuda") if gemma else None
+    ca.attention_block_dev(
+        *(x.to(torch.bfloat16).cuda() for x in (q, k, v)), batch=B, n_active=0,
+        active_pos=torch.from_numpy(pos.astype(np.int32)).cuda(),
+        rope=torch.from_numpy(rope).cuda(), rope_len=4096, rope_dim=hd, cache_k=cache_k,
+        cache_v=cache_v, n_total=0, q_work=q_work, out=out, n_head=H, n_head_kv=Hkv,
+        head_dim=hd, q_norm_w=None if wq is None else wq.cuda(),
+        k_norm_w=None if wk is None else wk.cuda(), v_norm=v_norm, rms_eps=eps, out_f32=True,
+        scale=scale, precise=True, cu_active=cu, cu_total=cu, max_active=max(lens),
+        total_active=n, total_cache=n, seq_prefix=prefix_d)
+    torch.cuda.synchronize()
+    assert ca.device_status() == ca.CA_OK
+    qq, kk, vv = _oracle_block(q.numpy().reshape(-1), k.numpy().reshape(-1),
+                               v.numpy().reshape(-1), pos, None if wq is None else wq.numpy(),
+                               None if wk is None else wk.numpy(), rope, hd, H, Hkv, hd, eps)
+    if v_norm:
+        vv = bf16_round(torch.from_numpy(_norm_v_heads(vv, hd, eps))).numpy()
+    np.testing.assert_allclose(cache_k.float().cpu().numpy().reshape(-1), kk, atol=1e-2,
+                               rtol=1e-2)
+    prefix = np.array([starts[s_] for s_ in seq]) if gemma else None
+    ref = oracle_attention(qq, kk, vv, nq=n, nk=n, h=H, hkv=Hkv, hd=hd, q_pos=pos, k_pos=pos,
+                           q_seq=seq, k_seq=seq, q_prefix=prefix, scale=scale)
+    check_close(out.cpu().numpy(), ref, H, hd, what=f"varlen block hd={hd} gemma={gemma}")
