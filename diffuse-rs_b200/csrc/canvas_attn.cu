@@ -7,6 +7,7 @@
 #include <climits>
 #include <cmath>
 #include <cstdint>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -14,6 +15,7 @@
 #include "canvas_attn.h"
 #include "attn_fwd.cuh"
 #include "prep.cuh"
+#include "sampler.cuh"
 
 namespace ca {
 namespace {
@@ -828,6 +830,56 @@ int ca_ipc_close(void* dev_ptr) {
   }
   if (!base) return CA_ERR_INVALID;
   return cudaIpcCloseMemHandle(base) == cudaSuccess ? CA_OK : CA_ERR_CUDA;
+}
+
+int ca_candidate_stats(const ca_cand_args* a, void* stream) {
+  if (!a || !a->logits || !a->rows || !a->token || a->n_cand < 0 || a->n_vocab <= 0 ||
+      a->n_vocab > INT_MAX || a->n_suppress < 0 || (a->n_suppress > 0 && !a->suppress))
+    return CA_ERR_INVALID;
+  if ((a->want_entropy && !a->entropy) || (a->want_prob && !a->prob)) return CA_ERR_INVALID;
+  const int64_t rs = a->row_stride ? a->row_stride : a->n_vocab;
+  if (rs < a->n_vocab) return CA_ERR_INVALID;
+  if (a->n_cand == 0) return CA_OK;
+  ca::CandParams p{};
+  p.logits = a->logits;
+  p.n_vocab = a->n_vocab;
+  p.row_stride = rs;
+  p.rows = a->rows;
+  p.n_cand = a->n_cand;
+  p.mask_id = a->mask_id;
+  p.suppress = a->suppress;
+  p.n_suppress = a->n_suppress;
+  p.want_entropy = a->want_entropy;
+  p.want_prob = a->want_prob;
+  p.token = a->token;
+  p.entropy = a->entropy;
+  p.margin = a->margin;
+  p.prob = a->prob;
+  ca::cand_stats_kernel<<<a->n_cand, ca::kCandThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
+}
+
+// tokens_to_unmask (src/model/sampler.rs:115-132) in f32 as the reference.
+int64_t ca_tokens_to_unmask(int64_t step, int64_t total_steps, int64_t masked, int32_t schedule) {
+  if (step < 0 || total_steps < 0 || masked < 0 || (schedule != 0 && schedule != 1))
+    return CA_ERR_INVALID;
+  const int64_t steps_left = std::max<int64_t>(total_steps > step ? total_steps - step : 0, 1);
+  const float t0 = static_cast<float>(step) / static_cast<float>(total_steps);
+  const float t1 = static_cast<float>(step + 1) / static_cast<float>(total_steps);
+  float frac;
+  if (schedule == CA_SCHEDULE_COSINE) {
+    const float half_pi = 1.57079632679489661923f;
+    const float c0 = std::max(cosf(t0 * half_pi), 1e-6f);
+    const float c1 = cosf(t1 * half_pi);
+    frac = (c0 - c1) / c0;
+  } else {
+    frac = 1.0f / static_cast<float>(steps_left);
+  }
+  const float nf = roundf(frac * static_cast<float>(masked));
+  // `as usize` saturates: NaN and negatives become 0.
+  int64_t n = (nf != nf || nf <= 0.f) ? 0 : static_cast<int64_t>(nf);
+  n = std::max<int64_t>(n, masked > 0 ? 1 : 0);
+  return std::min<int64_t>(n, masked);
 }
 
 int ca_selftest_wait_timeout(int64_t limit_ns, void* stream) {

@@ -251,6 +251,49 @@ int ca_ipc_export(const void* dev_ptr, void* handle, uint64_t* offset);
 int ca_ipc_import(const void* handle, uint64_t offset, void** dev_ptr);
 int ca_ipc_close(void* dev_ptr);
 
+/* Arguments of ca_candidate_stats (device pointers unless noted). */
+typedef struct {
+    float* logits;            /* fp32 [rows, row_stride]: the step's logits */
+    int64_t n_vocab;
+    int64_t row_stride;       /* elements between rows; 0 = n_vocab */
+    const int32_t* rows;      /* int32 [n_cand]: logit row of each candidate
+                                 (its position minus the model's logit shift) */
+    int32_t n_cand;
+    int32_t mask_id;          /* mask token id, or < 0 for none */
+    const int32_t* suppress;  /* int32 [n_suppress] token ids never committed, or NULL */
+    int32_t n_suppress;
+    int32_t want_entropy;     /* 0: entropy written as 0 (as the reference when unused) */
+    int32_t want_prob;        /* 0: prob written as 0 */
+    int32_t* token;           /* int32 [n_cand] out: greedy pick */
+    float* entropy;           /* fp32 [n_cand] out (may be NULL when !want_entropy) */
+    float* margin;            /* fp32 [n_cand] out: top1 - top2 (may be NULL) */
+    float* prob;              /* fp32 [n_cand] out (may be NULL when !want_prob) */
+} ca_cand_args;
+
+/*
+ * ca_candidate_stats -- replaces the per-candidate loop of
+ * Denoiser::collect_candidates (src/model/sampler.rs:720-749) for the greedy
+ * pick (pick_token, temperature 0, :754-764), after suppress_mask_token and
+ * suppress_tokens (:90-113), on logits resident in HBM: one launch per
+ * step, asynchronous on `stream`. For candidate i, over logit row rows[i]:
+ * token = first index of the maximum (0 if every entry is -inf), margin =
+ * top1 - top2 (top2_logits :75-87), entropy = compute_entropy (:7-20, the
+ * p > 1e-10 rule included), prob = exp(top1 - log_sum_exp) (:22-25). As in
+ * the reference, the mask token and the suppressed ids of the candidate rows
+ * are set to -inf in `logits` itself. Sums are formed in a different order
+ * than the reference's sequential f32 folds (results agree to ~1e-6
+ * relative); token and margin are exact. Allocates nothing.
+ */
+int ca_candidate_stats(const ca_cand_args* a, void* stream);
+
+/* tokens_to_unmask (src/model/sampler.rs:115-132), host, in the reference's
+ * f32 arithmetic: how many of `masked` remaining tokens to commit at `step`
+ * of `total_steps`. Returns the count, or CA_ERR_INVALID. */
+#define CA_SCHEDULE_COSINE 0
+#define CA_SCHEDULE_LINEAR 1
+int64_t ca_tokens_to_unmask(int64_t step, int64_t total_steps, int64_t masked,
+                            int32_t schedule);
+
 /*
  * ca_build_rope_table -- replaces build_rope_cache_ff (src/model/ops.rs:398-416),
  * host side, run once at load like the reference. out: host fp32

@@ -7,7 +7,7 @@ baseline -- never by the product package.
 
 Every function mirrors one reference function; the C source cites the
 reference file:line for each (src/model/attention.rs, src/model/ops.rs,
-src/model/cache.rs).
+src/model/cache.rs, src/model/sampler.rs).
 """
 from __future__ import annotations
 
@@ -84,6 +84,20 @@ def lib():
                                      ctypes.c_int64, ctypes.c_int64]
         L.or_cache_store.argtypes = [fp, fp, ctypes.c_int64, ip, ctypes.c_int64, fp, fp]
         L.or_cache_gather.argtypes = [fp, fp, ctypes.c_int64, ip, ctypes.c_int64, fp, fp]
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        L.or_compute_entropy.argtypes = [fp, ctypes.c_int64]
+        L.or_compute_entropy.restype = ctypes.c_float
+        L.or_log_sum_exp.argtypes = [fp, ctypes.c_int64]
+        L.or_log_sum_exp.restype = ctypes.c_float
+        L.or_top2_logits.argtypes = [fp, ctypes.c_int64, fp, fp]
+        L.or_pick_greedy.argtypes = [fp, ctypes.c_int64]
+        L.or_pick_greedy.restype = ctypes.c_int32
+        L.or_candidate_stats.argtypes = [fp, ctypes.c_int64, ctypes.c_int64, i32p,
+                                         ctypes.c_int64, ctypes.c_int32, i32p, ctypes.c_int64,
+                                         ctypes.c_int, ctypes.c_int, i32p, fp, fp, fp]
+        L.or_tokens_to_unmask.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                          ctypes.c_int32]
+        L.or_tokens_to_unmask.restype = ctypes.c_int64
         L.or_have_avx2.restype = ctypes.c_int
         L.or_max_threads.restype = ctypes.c_int
         _lib = L
@@ -225,3 +239,47 @@ def have_avx2() -> bool:
 
 def max_threads() -> int:
     return int(lib().or_max_threads())
+
+
+# ---------------------------------------------------------------- sampler
+def compute_entropy(row):
+    row, rp = _f32(row)
+    return float(lib().or_compute_entropy(rp, len(row)))
+
+
+def log_sum_exp(row):
+    row, rp = _f32(row)
+    return float(lib().or_log_sum_exp(rp, len(row)))
+
+
+def top2_logits(row):
+    row, rp = _f32(row)
+    t1, t2 = ctypes.c_float(), ctypes.c_float()
+    lib().or_top2_logits(rp, len(row), ctypes.byref(t1), ctypes.byref(t2))
+    return float(t1.value), float(t2.value)
+
+
+def candidate_stats(logits, rows, *, mask_id=-1, suppress=(), want_entropy=True,
+                    want_prob=True):
+    """collect_candidates' per-row statistics (greedy pick) on a copy of
+    `logits` [rows_total, n_vocab]; returns (token, entropy, margin, prob)."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    n_rows, n_vocab = lg.shape
+    rows = np.ascontiguousarray(rows, dtype=np.int32)
+    sup = np.ascontiguousarray(suppress, dtype=np.int32)
+    n = len(rows)
+    tok = np.zeros(n, np.int32)
+    ent, mar, prob = (np.zeros(n, np.float32) for _ in range(3))
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    fp = ctypes.POINTER(ctypes.c_float)
+    lib().or_candidate_stats(lg.ctypes.data_as(fp), n_rows, n_vocab, rows.ctypes.data_as(i32p),
+                             n, int(mask_id), sup.ctypes.data_as(i32p), len(sup),
+                             int(want_entropy), int(want_prob), tok.ctypes.data_as(i32p),
+                             ent.ctypes.data_as(fp), mar.ctypes.data_as(fp),
+                             prob.ctypes.data_as(fp))
+    return tok, ent, mar, prob
+
+
+def tokens_to_unmask(step, total_steps, masked, schedule):
+    """schedule: 0 cosine, 1 linear (src/model/sampler.rs:115-132)."""
+    return int(lib().or_tokens_to_unmask(step, total_steps, masked, schedule))

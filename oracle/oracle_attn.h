@@ -91,6 +91,19 @@ int or_have_avx2(void);
 /* Number of OpenMP threads a call with threads<=0 uses. */
 int or_max_threads(void);
 
+/* Denoising-step statistics (oracle_sampler.c, src/model/sampler.rs). */
+float or_compute_entropy(const float* row, int64_t n);
+float or_log_sum_exp(const float* row, int64_t n);
+void or_top2_logits(const float* row, int64_t n, float* top1, float* top2);
+int32_t or_pick_greedy(const float* row, int64_t n);
+void or_candidate_stats(float* logits, int64_t rows_total, int64_t n_vocab,
+                        const int32_t* rows, int64_t n_cand, int32_t mask_id,
+                        const int32_t* suppress, int64_t n_suppress, int want_entropy,
+                        int want_prob, int32_t* token, float* entropy, float* margin,
+                        float* prob);
+int64_t or_tokens_to_unmask(int64_t step, int64_t total_steps, int64_t masked,
+                            int32_t schedule);
+
 #ifdef __cplusplus
 }
 #endif
