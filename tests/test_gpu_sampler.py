@@ -6,8 +6,12 @@ process_logits step of the host mirror against the same step built on the
 oracle's statistics.
 
 Bar: token and margin exact (margin is one subtraction of two exact
-maxima); entropy within 1e-4 absolute + 1e-4 relative and prob within 1e-5
-absolute + 1e-4 relative (f32 sums formed in another order)."""
+maxima); entropy within 1e-4 absolute + 1e-4 relative. prob = exp(top1 -
+log_sum_exp) inherits the relative error of the row's sum of exponentials,
+which the reference folds sequentially in f32: over 10^5 terms that sum
+itself is off by up to ~5e-4 relative. So prob must lie within 1e-5 + 2e-3
+relative of the oracle AND be at least as close to the float64 value as the
+oracle is (to 1e-6)."""
 import numpy as np
 import pytest
 import torch
@@ -42,13 +46,28 @@ def _gpu_stats(lg, rows, *, mask_id=-1, suppress=(), row_stride=0, want_prob=Tru
             d.cpu().numpy()[:, :vocab])
 
 
-def _check(got, ref, what):
+def _prob64(lg, rows, mask_id=-1, suppress=()):
+    """exp(top1 - log_sum_exp) of each row in float64, after suppression."""
+    x = np.array(lg, dtype=np.float64)
+    for i in [mask_id, *suppress]:
+        if 0 <= i < x.shape[1]:
+            x[:, i] = -np.inf
+    out = []
+    for r in rows:
+        m = x[r].max()
+        out.append(np.exp(m - (m + np.log(np.exp(x[r] - m).sum()))))
+    return np.array(out)
+
+
+def _check(got, ref, what, p64=None):
     tok, ent, mar, prob = got[:4]
     rt, re_, rm, rp = ref
     np.testing.assert_array_equal(tok, rt, err_msg=f"{what}: token")
     np.testing.assert_array_equal(mar, rm, err_msg=f"{what}: margin")
     np.testing.assert_allclose(ent, re_, atol=1e-4, rtol=1e-4, err_msg=f"{what}: entropy")
-    np.testing.assert_allclose(prob, rp, atol=1e-5, rtol=1e-4, err_msg=f"{what}: prob")
+    np.testing.assert_allclose(prob, rp, atol=1e-5, rtol=2e-3, err_msg=f"{what}: prob")
+    if p64 is not None:
+        assert (np.abs(prob - p64) <= np.abs(rp - p64) + 1e-6).all(), f"{what}: prob vs f64"
 
 
 @pytest.mark.parametrize("vocab,row_stride", [(16, 0), (1001, 0), (126464, 0),
@@ -61,7 +80,7 @@ def test_candidate_stats_match_oracle(vocab, row_stride):
     mask_id, suppress = vocab - 1, (1, 2, vocab // 2)
     got = _gpu_stats(lg, rows, mask_id=mask_id, suppress=suppress, row_stride=row_stride)
     ref = orc.candidate_stats(lg, rows, mask_id=mask_id, suppress=suppress)
-    _check(got, ref, f"vocab {vocab}")
+    _check(got, ref, f"vocab {vocab}", _prob64(lg, rows, mask_id, suppress))
     # Suppressed entries of the candidate rows are -inf in the buffer afterwards.
     after = got[4]
     assert np.isneginf(after[rows][:, [1, 2, vocab // 2, vocab - 1]]).all()
