@@ -40,6 +40,8 @@ EXPORTED_SYMBOLS = (
     "ca_attention_block_dev",
     "ca_attention_block_dev_noalloc",
     "ca_build_rope_table",
+    "ca_dequantize",
+    "ca_linear",
     "ca_candidate_stats",
     "ca_tokens_to_unmask",
     "ca_ipc_export",

@@ -16,6 +16,8 @@
 #include "attn_fwd.cuh"
 #include "prep.cuh"
 #include "sampler.cuh"
+#include "quant.cuh"
+#include <cublasLt.h>
 
 namespace ca {
 namespace {
@@ -880,6 +882,131 @@ int64_t ca_tokens_to_unmask(int64_t step, int64_t total_steps, int64_t masked, i
   int64_t n = (nf != nf || nf <= 0.f) ? 0 : static_cast<int64_t>(nf);
   n = std::max<int64_t>(n, masked > 0 ? 1 : 0);
   return std::min<int64_t>(n, masked);
+}
+
+int ca_dequantize(int32_t qtype, const void* src, int64_t rows, int64_t cols,
+                  const int32_t* row_ids, int64_t n_out, void* dst, int32_t dst_f32,
+                  int64_t dst_stride, float scale, int32_t* status, void* stream) {
+  using namespace ca;
+  if (!src || !dst || rows < 0 || cols <= 0 || n_out < 0) return CA_ERR_INVALID;
+  const int64_t unit = qtype == kQ4_K || qtype == kQ6_K ? 256
+                       : qtype == kQ4_0 || qtype == kQ8_0 ? 32
+                       : qtype == kQF16 ? 8 : 0;
+  if (!unit) return CA_ERR_UNSUPPORTED;
+  if (cols % unit) return CA_ERR_INVALID;
+  const int64_t ds = dst_stride ? dst_stride : cols;
+  if (ds < cols || ds % 8 || (reinterpret_cast<uintptr_t>(dst) & 15u)) return CA_ERR_INVALID;
+  if (!row_ids && n_out > rows) return CA_ERR_INVALID;
+  if (n_out == 0) return CA_OK;
+  DequantParams p{};
+  p.src = static_cast<const uint8_t*>(src);
+  p.rows = rows;
+  p.cols = cols;
+  p.row_ids = row_ids;
+  p.n_out = n_out;
+  p.dst = dst;
+  p.dst_f32 = dst_f32 ? 1 : 0;
+  p.dst_stride = ds;
+  p.scale = scale;
+  p.qtype = qtype;
+  p.err = status;
+  const long long warps = n_out * ((cols + 255) / 256);
+  const int blocks = static_cast<int>(std::min<long long>((warps + 7) / 8, 148LL * 16));
+  dequant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
+}
+
+}  // extern "C"
+
+namespace ca {
+namespace {
+
+// cuBLASLt state of one device: handle and a 32 MiB workspace, created on
+// first use and kept for the process lifetime.
+struct LtCtx {
+  std::mutex mu;
+  cublasLtHandle_t h = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+LtCtx g_lt[kMaxDevices];
+
+int linear_impl(const ca_linear_args* a, cudaStream_t st) {
+  if (!a || !a->act || !a->w || !a->out || a->n < 0 || a->rows <= 0 || a->cols <= 0)
+    return CA_ERR_INVALID;
+  if (a->n == 0) return CA_OK;
+  const int64_t as = a->act_stride ? a->act_stride : a->cols;
+  if (as < a->cols) return CA_ERR_INVALID;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
+  LtCtx& c = g_lt[dev];
+  std::lock_guard<std::mutex> lock(c.mu);
+  if (!c.h) {
+    if (cublasLtCreate(&c.h) != CUBLAS_STATUS_SUCCESS) return CA_ERR_CUDA;
+    c.ws_bytes = 32u << 20;
+    if (cudaMalloc(&c.ws, c.ws_bytes) != cudaSuccess) {
+      c.ws = nullptr;
+      c.ws_bytes = 0;
+    }
+  }
+  // Row-major out[n, rows] = act[n, cols] . W[rows, cols]^T is, column-major,
+  // D[rows, n] = W^T(op T on a [cols, rows] matrix) x act^T ([cols, n]).
+  const cudaDataType_t dt = a->out_f32 ? CUDA_R_32F : CUDA_R_16BF;
+  cublasLtMatmulDesc_t op = nullptr;
+  cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+  cublasLtMatmulPreference_t pref = nullptr;
+  int rc = CA_ERR_CUDA;
+  do {
+    if (cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F) != CUBLAS_STATUS_SUCCESS) break;
+    const cublasOperation_t tA = CUBLAS_OP_T, tB = CUBLAS_OP_N;
+    cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &tA, sizeof(tA));
+    cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tB, sizeof(tB));
+    if (a->bias) {
+      const cublasLtEpilogue_t ep = CUBLASLT_EPILOGUE_BIAS;
+      const cudaDataType_t bt = CUDA_R_32F;
+      cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_EPILOGUE, &ep, sizeof(ep));
+      cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &a->bias,
+                                     sizeof(a->bias));
+      cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bt, sizeof(bt));
+    }
+    if (cublasLtMatrixLayoutCreate(&la, CUDA_R_16BF, a->cols, a->rows, a->cols) !=
+            CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatrixLayoutCreate(&lb, CUDA_R_16BF, a->cols, a->n, as) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatrixLayoutCreate(&lc, dt, a->rows, a->n, a->rows) != CUBLAS_STATUS_SUCCESS)
+      break;
+    if (cublasLtMatmulPreferenceCreate(&pref) != CUBLAS_STATUS_SUCCESS) break;
+    cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES,
+                                         &c.ws_bytes, sizeof(c.ws_bytes));
+    cublasLtMatmulHeuristicResult_t heur;
+    int found = 0;
+    if (cublasLtMatmulAlgoGetHeuristic(c.h, op, la, lb, lc, lc, pref, 1, &heur, &found) !=
+            CUBLAS_STATUS_SUCCESS ||
+        found == 0) {
+      rc = CA_ERR_UNSUPPORTED;
+      break;
+    }
+    const float alpha = 1.f, beta = a->residual ? 1.f : 0.f;
+    const void* cptr = a->residual ? a->residual : a->out;
+    if (cublasLtMatmul(c.h, op, &alpha, a->w, la, a->act, lb, &beta, cptr, lc, a->out, lc,
+                       &heur.algo, c.ws, c.ws_bytes, st) != CUBLAS_STATUS_SUCCESS)
+      break;
+    rc = CA_OK;
+  } while (false);
+  if (pref) cublasLtMatmulPreferenceDestroy(pref);
+  if (lc) cublasLtMatrixLayoutDestroy(lc);
+  if (lb) cublasLtMatrixLayoutDestroy(lb);
+  if (la) cublasLtMatrixLayoutDestroy(la);
+  if (op) cublasLtMatmulDescDestroy(op);
+  return rc;
+}
+
+}  // namespace
+}  // namespace ca
+
+extern "C" {
+
+int ca_linear(const ca_linear_args* a, void* stream) {
+  return ca::linear_impl(a, static_cast<cudaStream_t>(stream));
 }
 
 int ca_selftest_wait_timeout(int64_t limit_ns, void* stream) {

@@ -1,0 +1,144 @@
+// quant.cuh -- GGUF block formats of the reference's weights, dequantised on
+// the GPU: Q4_K, Q6_K, Q4_0, Q8_0 and F16 rows to bf16 or fp32
+// (dequantize_q4k_row / _q6k_row / _q4_0_row / _q8_0_row and f16_to_f32,
+// src/kernels.rs:46-217). Used once at load for projection weights (the
+// projections then run as bf16 GEMMs with fp32 accumulation) and per step
+// for the token-embedding gather (embed_tokens, src/model/forward.rs:
+// 175-246). Byte/integer work, HBM-bound: one warp per 256 weights, each
+// lane producing 8 consecutive outputs with one 16- or 32-byte store. The
+// f32 arithmetic is the reference's, operation for operation (no
+// contraction), so fp32 outputs are bit-identical to it.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace ca {
+
+enum QType { kQF16 = 1, kQ4_0 = 2, kQ8_0 = 8, kQ4_K = 12, kQ6_K = 14 };
+
+__host__ __device__ constexpr long long qrow_bytes(int qtype, long long cols) {
+  return qtype == kQF16   ? 2 * cols
+         : qtype == kQ4_0 ? cols / 32 * 18
+         : qtype == kQ8_0 ? cols / 32 * 34
+         : qtype == kQ4_K ? cols / 256 * 144
+         : qtype == kQ6_K ? cols / 256 * 210
+                          : 0;
+}
+
+struct DequantParams {
+  const uint8_t* src;   // rows of qrow_bytes(qtype, cols) bytes
+  long long rows, cols;
+  const int* row_ids;   // output row i <- source row row_ids[i] (null: i)
+  long long n_out;
+  void* dst;            // [n_out, dst_stride]
+  int dst_f32;
+  long long dst_stride;
+  float scale;          // applied after dequantisation (1: none)
+  int qtype;
+  int* err;             // set when a row id is out of range
+};
+
+__device__ __forceinline__ float h2f(const uint8_t* p) {
+  const unsigned short h = static_cast<unsigned short>(p[0] | (p[1] << 8));
+  return __half2float(__ushort_as_half(h));  // exact, subnormals included
+}
+
+// The 6-bit scale (which = 0) or min (which = 1) of sub-block j of a Q4_K
+// block, from its 12 packed bytes (the utmp unpacking of the reference).
+__device__ __forceinline__ int q4k_scale(const uint8_t* s, int j, int which) {
+  if (j < 4) return which ? (s[j + 4] & 63) : (s[j] & 63);
+  return which ? ((s[j + 4] >> 4) | ((s[j] >> 6) << 4)) : ((s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4));
+}
+
+// Eight consecutive weights idx .. idx + 7 (idx % 8 == 0) of one row.
+__device__ __forceinline__ void dequant8(int qtype, const uint8_t* row, int idx, float (&o)[8]) {
+  if (qtype == kQ4_K) {
+    const uint8_t* b = row + (idx >> 8) * 144;
+    const int v = idx & 255;
+    const int pair = v >> 6, w = v & 63;  // 64 weights share one byte range
+    const int sub = 2 * pair + (w >= 32 ? 1 : 0);
+    const float d = h2f(b), dmin = h2f(b + 2);
+    const float sc = static_cast<float>(q4k_scale(b + 4, sub, 0));
+    const float mn = static_cast<float>(q4k_scale(b + 4, sub, 1));
+    const uint8_t* qs = b + 16 + pair * 32 + (w & 31);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int q = w >= 32 ? (qs[k] >> 4) : (qs[k] & 0xF);
+      // d * sc * q - dmin * mn, left to right, no contraction
+      o[k] = __fsub_rn(__fmul_rn(__fmul_rn(d, sc), static_cast<float>(q)), __fmul_rn(dmin, mn));
+    }
+  } else if (qtype == kQ6_K) {
+    const uint8_t* b = row + (idx >> 8) * 210;
+    const int v = idx & 255;
+    const int h = v >> 7, g = (v & 127) >> 5, l0 = v & 31;
+    const uint8_t* ql = b + h * 64 + (g & 1) * 32 + l0;
+    const uint8_t* qh = b + 128 + h * 32 + l0;
+    const float sc = __fmul_rn(h2f(b + 208), static_cast<float>(static_cast<int8_t>(b[192 + (v >> 4)])));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int lo = g < 2 ? (ql[k] & 0xF) : (ql[k] >> 4);
+      const int hi = (qh[k] >> (2 * g)) & 3;
+      o[k] = __fmul_rn(sc, static_cast<float>((lo | (hi << 4)) - 32));
+    }
+  } else if (qtype == kQ4_0) {
+    const uint8_t* b = row + (idx >> 5) * 18;
+    const int w = idx & 31;
+    const float d = h2f(b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int q = w < 16 ? (b[2 + w + k] & 0xF) : (b[2 + w - 16 + k] >> 4);
+      o[k] = __fmul_rn(d, __fsub_rn(static_cast<float>(q), 8.0f));
+    }
+  } else if (qtype == kQ8_0) {
+    const uint8_t* b = row + (idx >> 5) * 34;
+    const float d = h2f(b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      o[k] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(b[2 + (idx & 31) + k])));
+  } else {  // F16
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = h2f(row + 2 * (idx + k));
+  }
+}
+
+// One warp per 256 output weights of one output row (grid-stride).
+__global__ void __launch_bounds__(256) dequant_kernel(const DequantParams p) {
+  const int lane = threadIdx.x & 31;
+  const long long units_per_row = (p.cols + 255) / 256;
+  const long long units = p.n_out * units_per_row;
+  const long long rb = qrow_bytes(p.qtype, p.cols);
+  for (long long u = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       u < units; u += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const long long i = u / units_per_row;
+    const int idx = static_cast<int>((u % units_per_row) * 256 + lane * 8);
+    if (idx >= p.cols) continue;
+    const long long r = p.row_ids ? p.row_ids[i] : i;
+    if (r < 0 || r >= p.rows) {
+      if (lane == 0 && p.err) atomicExch(p.err, 1);
+      continue;
+    }
+    float o[8];
+    dequant8(p.qtype, p.src + r * rb, idx, o);
+    if (p.scale != 1.f) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(o[k], p.scale);
+    }
+    const long long off = i * p.dst_stride + idx;
+    if (p.dst_f32) {
+      float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.dst) + off);
+      d[0] = make_float4(o[0], o[1], o[2], o[3]);
+      d[1] = make_float4(o[4], o[5], o[6], o[7]);
+    } else {
+      uint4 w;
+      w.x = pack_bf16(o[0], o[1]);
+      w.y = pack_bf16(o[2], o[3]);
+      w.z = pack_bf16(o[4], o[5]);
+      w.w = pack_bf16(o[6], o[7]);
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.dst) + off) = w;
+    }
+  }
+}
+
+}  // namespace ca

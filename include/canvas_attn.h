@@ -295,6 +295,64 @@ int64_t ca_tokens_to_unmask(int64_t step, int64_t total_steps, int64_t masked,
                             int32_t schedule);
 
 /*
+ * Projections around attention (src/model/forward.rs:275-294 QKV + bias,
+ * :345-350 wo + residual) over the reference's quantised weights. The
+ * weights are dequantised once (ca_dequantize, bit-identical in f32 to
+ * dequantize_q4k_row / _q6k_row / _q4_0_row / _q8_0_row / f16_to_f32,
+ * src/kernels.rs:46-217) and kept in HBM as bf16; each projection is then
+ * one bf16 GEMM with fp32 accumulation (ca_linear). The reference instead
+ * quantises the activations of Q4_K / Q6_K products to 8 bits per 256-value
+ * block (src/model/matmul.rs:90-151); bf16 activations are closer to the
+ * exact product than that.
+ */
+#define CA_QTYPE_F16 1
+#define CA_QTYPE_Q4_0 2
+#define CA_QTYPE_Q8_0 8
+#define CA_QTYPE_Q4_K 12
+#define CA_QTYPE_Q6_K 14
+
+/*
+ * ca_dequantize -- rows of GGUF blocks to bf16 (dst_f32 = 0) or fp32 on the
+ * device, asynchronous on `stream`. src: `rows` rows of `cols` weights of
+ * type qtype (device memory, rows packed back to back). Output row i (of
+ * n_out) is source row row_ids[i] (device int32, e.g. token ids: the
+ * embedding gather of embed_tokens, src/model/forward.rs:175-246), or row i
+ * when row_ids is NULL, times `scale` (1 = none; Gemma's embed_scale).
+ * dst: 16-byte aligned, row stride dst_stride elements (0 = cols, a
+ * multiple of 8). cols must be a multiple of 256 (Q4_K, Q6_K), 32 (Q4_0,
+ * Q8_0) or 8 (F16). A row id out of range skips that row and sets *status
+ * (device int32, may be NULL) to 1.
+ */
+int ca_dequantize(int32_t qtype, const void* src, int64_t rows, int64_t cols,
+                  const int32_t* row_ids, int64_t n_out, void* dst, int32_t dst_f32,
+                  int64_t dst_stride, float scale, int32_t* status, void* stream);
+
+/* Arguments of ca_linear (device pointers). */
+typedef struct {
+    const void* act;       /* bf16 [n, cols], row stride act_stride (0 = cols) */
+    int64_t act_stride;
+    const void* w;         /* bf16 [rows, cols] (e.g. from ca_dequantize) */
+    const float* bias;     /* fp32 [rows] or NULL (add_bias, forward.rs:292-294) */
+    const void* residual;  /* [n, rows] of out's type or NULL (residual_add,
+                              forward.rs:350); may be the same buffer as out */
+    void* out;             /* [n, rows]: bf16, or fp32 when out_f32 */
+    int32_t out_f32;
+    int64_t n;
+    int64_t rows;
+    int64_t cols;
+} ca_linear_args;
+
+/*
+ * ca_linear -- replaces MatWeight::forward (src/model/matmul.rs:90-110,
+ * out[t*rows + r] = act row t . weight row r) with the bias and residual
+ * adds around it: out = act . W^T (+ bias) (+ residual), bf16 operands,
+ * fp32 accumulation, one cuBLASLt GEMM with the bias and residual in its
+ * epilogue, asynchronous on `stream`. The first call on a device creates a
+ * cuBLASLt handle and a 32 MiB workspace that the library keeps.
+ */
+int ca_linear(const ca_linear_args* a, void* stream);
+
+/*
  * ca_build_rope_table -- replaces build_rope_cache_ff (src/model/ops.rs:398-416),
  * host side, run once at load like the reference. out: host fp32
  * [max_seq_len, rope_dim/2, 2] as (sin, cos); freq_factors may be NULL.

@@ -7,7 +7,7 @@ baseline -- never by the product package.
 
 Every function mirrors one reference function; the C source cites the
 reference file:line for each (src/model/attention.rs, src/model/ops.rs,
-src/model/cache.rs, src/model/sampler.rs).
+src/model/cache.rs, src/model/sampler.rs, src/kernels.rs, src/model/matmul.rs).
 """
 from __future__ import annotations
 
@@ -98,6 +98,23 @@ def lib():
         L.or_tokens_to_unmask.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                           ctypes.c_int32]
         L.or_tokens_to_unmask.restype = ctypes.c_int64
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        L.or_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.or_f16_to_f32.restype = ctypes.c_float
+        L.or_dequant_row.argtypes = [ctypes.c_int32, u8p, ctypes.c_int64, fp]
+        L.or_dequant_row.restype = ctypes.c_int
+        L.or_row_bytes.argtypes = [ctypes.c_int32, ctypes.c_int64]
+        L.or_row_bytes.restype = ctypes.c_int64
+        L.or_quantize_row_q8k.argtypes = [fp, ctypes.c_int64, fp, ctypes.POINTER(ctypes.c_int8),
+                                          ctypes.POINTER(ctypes.c_int16)]
+        L.or_vec_dot_q4k_q8k.argtypes = [u8p, fp, ctypes.POINTER(ctypes.c_int8),
+                                         ctypes.POINTER(ctypes.c_int16), ctypes.c_int64]
+        L.or_vec_dot_q4k_q8k.restype = ctypes.c_float
+        L.or_vec_dot_q6k_q8k.argtypes = [u8p, fp, ctypes.POINTER(ctypes.c_int8), ctypes.c_int64]
+        L.or_vec_dot_q6k_q8k.restype = ctypes.c_float
+        L.or_linear_q8k.argtypes = [ctypes.c_int32, u8p, ctypes.c_int64, ctypes.c_int64, fp,
+                                    ctypes.c_int64, fp]
+        L.or_linear_q8k.restype = ctypes.c_int
         L.or_have_avx2.restype = ctypes.c_int
         L.or_max_threads.restype = ctypes.c_int
         _lib = L
@@ -283,3 +300,75 @@ def candidate_stats(logits, rows, *, mask_id=-1, suppress=(), want_entropy=True,
 def tokens_to_unmask(step, total_steps, masked, schedule):
     """schedule: 0 cosine, 1 linear (src/model/sampler.rs:115-132)."""
     return int(lib().or_tokens_to_unmask(step, total_steps, masked, schedule))
+
+
+# ---------------------------------------------------------------- quantised weights
+QTYPE_F16, QTYPE_Q4_0, QTYPE_Q8_0, QTYPE_Q4_K, QTYPE_Q6_K = 1, 2, 8, 12, 14
+
+
+def _u8(a):
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    return a, a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8))
+
+
+def f16_to_f32(h):
+    return float(lib().or_f16_to_f32(int(h)))
+
+
+def row_bytes(qtype, cols):
+    return int(lib().or_row_bytes(int(qtype), int(cols)))
+
+
+def dequantize(qtype, w_bytes, rows, cols):
+    """[rows, cols] f32 from `rows` rows of `cols` weights of type qtype."""
+    w, wp = _u8(w_bytes)
+    rb = row_bytes(qtype, cols)
+    out = np.zeros((rows, cols), np.float32)
+    fp = ctypes.POINTER(ctypes.c_float)
+    for r in range(rows):
+        rc = lib().or_dequant_row(int(qtype), ctypes.cast(ctypes.addressof(wp.contents) + r * rb,
+                                                           ctypes.POINTER(ctypes.c_uint8)),
+                                  int(cols), out[r].ctypes.data_as(fp))
+        if rc != 0:
+            raise ValueError(f"unknown qtype {qtype}")
+    return out
+
+
+def quantize_row_q8k(x):
+    x, xp = _f32(x)
+    nb = len(x) // 256
+    d = np.zeros(nb, np.float32)
+    qs = np.zeros(nb * 256, np.int8)
+    bs = np.zeros(nb * 16, np.int16)
+    lib().or_quantize_row_q8k(xp, nb, d.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                              qs.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)),
+                              bs.ctypes.data_as(ctypes.POINTER(ctypes.c_int16)))
+    return d, qs, bs
+
+
+def vec_dot_q4k_q8k(w_bytes, d, qs, bs):
+    w, wp = _u8(w_bytes)
+    return float(lib().or_vec_dot_q4k_q8k(wp, _f32(d)[1], qs.ctypes.data_as(
+        ctypes.POINTER(ctypes.c_int8)), bs.ctypes.data_as(ctypes.POINTER(ctypes.c_int16)),
+        len(d)))
+
+
+def vec_dot_q6k_q8k(w_bytes, d, qs):
+    w, wp = _u8(w_bytes)
+    return float(lib().or_vec_dot_q6k_q8k(wp, _f32(d)[1], qs.ctypes.data_as(
+        ctypes.POINTER(ctypes.c_int8)), len(d)))
+
+
+def linear_q8k(qtype, w_bytes, rows, cols, act):
+    """The reference's Q4_K / Q6_K projection (activations quantised to
+    Q8_K): [n, rows] f32 for act [n, cols]."""
+    w, wp = _u8(w_bytes)
+    act = np.ascontiguousarray(act, dtype=np.float32)
+    n = act.shape[0]
+    out = np.zeros((n, rows), np.float32)
+    rc = lib().or_linear_q8k(int(qtype), wp, int(rows), int(cols),
+                             act.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n,
+                             out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    if rc != 0:
+        raise ValueError("or_linear_q8k: unsupported type or width")
+    return out

@@ -104,6 +104,20 @@ void or_candidate_stats(float* logits, int64_t rows_total, int64_t n_vocab,
 int64_t or_tokens_to_unmask(int64_t step, int64_t total_steps, int64_t masked,
                             int32_t schedule);
 
+/* Quantised weight formats and projections (oracle_quant.c, src/kernels.rs,
+ * src/model/matmul.rs). qtype: GGML ids 1 F16, 2 Q4_0, 8 Q8_0, 12 Q4_K, 14 Q6_K. */
+float or_f16_to_f32(uint16_t h);
+int or_dequant_row(int32_t qtype, const uint8_t* row, int64_t cols, float* out);
+int64_t or_row_bytes(int32_t qtype, int64_t cols);
+void or_quantize_row_q8k(const float* x, int64_t n_blocks, float* d, int8_t* qs,
+                         int16_t* bsums);
+float or_vec_dot_q4k_q8k(const uint8_t* xb, const float* yd, const int8_t* yq,
+                         const int16_t* ybs, int64_t n_blocks);
+float or_vec_dot_q6k_q8k(const uint8_t* xb, const float* yd, const int8_t* yq,
+                         int64_t n_blocks);
+int or_linear_q8k(int32_t qtype, const uint8_t* w, int64_t rows, int64_t cols,
+                  const float* act, int64_t n, float* out);
+
 #ifdef __cplusplus
 }
 #endif
