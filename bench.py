@@ -518,6 +518,81 @@ def roofline(name, cfg, layers, ms, peaks, traffic_key=None):
     return r
 
 
+def _event_ms(fn, reps, flush=None):
+    """Average device time of fn() over reps calls (CUDA events, current stream)."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        tot += a.elapsed_time(b)
+    return tot / reps
+
+
+def run_extras(dev, peaks, scratch):
+    """Kernel-alone rooflines of the projection and sampler rows (synthetic
+    seeded data): Q4_K dequantisation of a 12288 x 4096 QKV weight
+    (LLaDA-8B: n_embd 4096, Q, K and V of 32 heads x 128 each), the bf16 QKV GEMM of
+    4096 tokens through it, and candidate statistics of 256 masked rows of a
+    126464-entry vocabulary (LLaDA's)."""
+    import numpy as np
+    import torch
+    from canvas_attn import denoise as dn
+    from canvas_attn import projection as pj
+    if scratch is None:
+        scratch = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    out = {}
+    rng = np.random.default_rng(11)
+    rows, cols, n = 12288, 4096, 4096
+    rb = pj.row_bytes(pj.Q4_K, cols)
+    wq = rng.integers(0, 256, (rows, rb), dtype=np.uint8)
+    blk = wq.reshape(-1, 144)
+    blk[:, 0:2] = np.float16(0.01).view(np.uint8)  # moderate d / dmin in every block
+    blk[:, 2:4] = np.float16(0.005).view(np.uint8)
+    src = torch.from_numpy(wq).to(dev)
+    w = torch.empty(rows, cols, dtype=torch.bfloat16, device=dev)
+    ms = _event_ms(lambda: pj.dequantize(pj.Q4_K, src, rows, cols, w), 20, scratch)
+    byt = rows * rb + rows * cols * 2
+    out["dequant_q4k"] = dict(bound="hbm", achieved=round(byt / (ms * 1e-3) / 1e9, 1),
+                              peak=peaks["hbm"], unit="GB/s", kernel_ms=round(ms, 4),
+                              shape=f"{rows}x{cols} Q4_K -> bf16",
+                              frac=round(byt / (ms * 1e-3) / 1e9 / peaks["hbm"], 4))
+    act = torch.randn(n, cols, device=dev).to(torch.bfloat16)
+    bias = torch.randn(rows, device=dev)
+    o = torch.empty(n, rows, device=dev)
+    ms = _event_ms(lambda: pj.linear(act, w, o, n=n, rows=rows, cols=cols, bias=bias), 20)
+    tf = 2.0 * n * rows * cols / (ms * 1e-3) / 1e12
+    out["linear_qkv"] = dict(bound="tensor", achieved=round(tf, 1), peak=peaks["tflops"],
+                             unit="TFLOP/s", kernel_ms=round(ms, 4), frac=round(tf / peaks["tflops"], 4),
+                             shape=f"[{n}, {cols}] x [{rows}, {cols}]^T + bias, fp32 out",
+                             gemm="cuBLASLt (library GEMM)")
+    del src, w, act, o
+    n_cand, vocab = 256, 126464
+    logits = torch.randn(n_cand + 8, vocab, device=dev) * 4
+    rows_t = torch.arange(n_cand, dtype=torch.int32, device=dev)
+    tok = torch.empty(n_cand, dtype=torch.int32, device=dev)
+    vals = torch.empty(3, n_cand, device=dev)
+    ms = _event_ms(lambda: dn.candidate_stats(logits, rows_t, tok, vals[0], vals[1], vals[2],
+                                              n_vocab=vocab, mask_id=vocab - 1,
+                                              want_entropy=True, want_prob=True), 20, scratch)
+    byt = n_cand * vocab * 4
+    out["candidate_stats"] = dict(bound="hbm", achieved=round(byt / (ms * 1e-3) / 1e9, 1),
+                                  peak=peaks["hbm"], unit="GB/s", kernel_ms=round(ms, 4),
+                                  frac=round(byt / (ms * 1e-3) / 1e9 / peaks["hbm"], 4),
+                                  shape=f"{n_cand} rows x {vocab} fp32 logits (entropy + prob)")
+    del logits
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_head_sharded(args, cfg, world, rank, dev):
     """Head-sharded strong scaling of ONE global batch of the config: rank r
     computes kv heads [r * Hkv / N, (r + 1) * Hkv / N) and their query heads
@@ -749,6 +824,13 @@ def run_ours(args, cfg):
             torch.cuda.synchronize()
         torch.cuda.empty_cache()
 
+    # The rows on either side of attention, on one GPU: weight dequantisation
+    # (HBM), the QKV projection GEMM (tensor) and the denoising step's
+    # per-candidate statistics (HBM).
+    extras = None
+    if world == 1 and not args.no_by_config:
+        extras = run_extras(dev, peaks, scratch)
+
     # Head sharding (N > 1): every rank computes its kv-head slice (and the
     # query heads of those groups) of ONE global batch of the config, then
     # one NCCL all-gather per layer reassembles full [tokens, n_head, hd]
@@ -796,6 +878,7 @@ def run_ours(args, cfg):
             "tokens_per_s": round(world * cfg["B"] * cfg["na"] * args.steps / (ms_total * 1e-3), 1),
             "roofline": roof,
             "roofline_by_config": by_config,
+            "roofline_extras": extras,
             "head_sharded": head_sharded,
             "cpu_baseline": cpu,
             "e2e": e2e,

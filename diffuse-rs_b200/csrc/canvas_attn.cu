@@ -921,15 +921,31 @@ int ca_dequantize(int32_t qtype, const void* src, int64_t rows, int64_t cols,
 namespace ca {
 namespace {
 
-// cuBLASLt state of one device: handle and a 32 MiB workspace, created on
-// first use and kept for the process lifetime.
+// cuBLASLt state of one device: handle, a 32 MiB workspace, and an fp32
+// accumulator buffer for bf16 outputs with a bias (grown on demand), created
+// on first use and kept for the process lifetime.
 struct LtCtx {
   std::mutex mu;
   cublasLtHandle_t h = nullptr;
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  float* acc = nullptr;
+  size_t acc_elems = 0;
 };
 LtCtx g_lt[kMaxDevices];
+
+// out[t, r] = bf16(acc[t, r] + bias[r] (+ residual[t, r])): one rounding.
+__global__ void bias_epilogue_kernel(const float* acc, const float* bias,
+                                     const __nv_bfloat16* residual, __nv_bfloat16* out,
+                                     long long n, long long rows) {
+  const long long total = n * rows;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float v = __fadd_rn(acc[i], bias[i % rows]);
+    if (residual) v = __fadd_rn(v, __bfloat162float(residual[i]));
+    out[i] = __float2bfloat16_rn(v);
+  }
+}
 
 int linear_impl(const ca_linear_args* a, cudaStream_t st) {
   if (!a || !a->act || !a->w || !a->out || a->n < 0 || a->rows <= 0 || a->cols <= 0)
@@ -949,9 +965,23 @@ int linear_impl(const ca_linear_args* a, cudaStream_t st) {
       c.ws_bytes = 0;
     }
   }
+  // bf16 output with a bias: cuBLASLt's bias epilogue wants a bf16 bias
+  // there, so the product goes to an fp32 buffer and one kernel adds the
+  // fp32 bias and the residual with a single rounding.
+  const bool split = !a->out_f32 && a->bias;
+  if (split) {
+    const size_t need = static_cast<size_t>(a->n) * static_cast<size_t>(a->rows);
+    if (need > c.acc_elems) {
+      if (c.acc) cudaFree(c.acc);
+      c.acc = nullptr;
+      c.acc_elems = 0;
+      if (cudaMalloc(&c.acc, need * sizeof(float)) != cudaSuccess) return CA_ERR_NOMEM;
+      c.acc_elems = need;
+    }
+  }
   // Row-major out[n, rows] = act[n, cols] . W[rows, cols]^T is, column-major,
   // D[rows, n] = W^T(op T on a [cols, rows] matrix) x act^T ([cols, n]).
-  const cudaDataType_t dt = a->out_f32 ? CUDA_R_32F : CUDA_R_16BF;
+  const cudaDataType_t dt = (a->out_f32 || split) ? CUDA_R_32F : CUDA_R_16BF;
   cublasLtMatmulDesc_t op = nullptr;
   cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
   cublasLtMatmulPreference_t pref = nullptr;
@@ -961,7 +991,7 @@ int linear_impl(const ca_linear_args* a, cudaStream_t st) {
     const cublasOperation_t tA = CUBLAS_OP_T, tB = CUBLAS_OP_N;
     cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &tA, sizeof(tA));
     cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tB, sizeof(tB));
-    if (a->bias) {
+    if (a->bias && !split) {
       const cublasLtEpilogue_t ep = CUBLASLT_EPILOGUE_BIAS;
       const cudaDataType_t bt = CUDA_R_32F;
       cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_EPILOGUE, &ep, sizeof(ep));
@@ -985,11 +1015,20 @@ int linear_impl(const ca_linear_args* a, cudaStream_t st) {
       rc = CA_ERR_UNSUPPORTED;
       break;
     }
-    const float alpha = 1.f, beta = a->residual ? 1.f : 0.f;
-    const void* cptr = a->residual ? a->residual : a->out;
-    if (cublasLtMatmul(c.h, op, &alpha, a->w, la, a->act, lb, &beta, cptr, lc, a->out, lc,
+    const float alpha = 1.f, beta = (a->residual && !split) ? 1.f : 0.f;
+    void* dptr = split ? static_cast<void*>(c.acc) : a->out;
+    const void* cptr = (a->residual && !split) ? a->residual : dptr;
+    if (cublasLtMatmul(c.h, op, &alpha, a->w, la, a->act, lb, &beta, cptr, lc, dptr, lc,
                        &heur.algo, c.ws, c.ws_bytes, st) != CUBLAS_STATUS_SUCCESS)
       break;
+    if (split) {
+      const long long total = a->n * a->rows;
+      const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+      bias_epilogue_kernel<<<blocks, 256, 0, st>>>(
+          c.acc, a->bias, static_cast<const __nv_bfloat16*>(a->residual),
+          static_cast<__nv_bfloat16*>(a->out), a->n, a->rows);
+      if (cudaGetLastError() != cudaSuccess) break;
+    }
     rc = CA_OK;
   } while (false);
   if (pref) cublasLtMatmulPreferenceDestroy(pref);

@@ -347,8 +347,11 @@ typedef struct {
  * out[t*rows + r] = act row t . weight row r) with the bias and residual
  * adds around it: out = act . W^T (+ bias) (+ residual), bf16 operands,
  * fp32 accumulation, one cuBLASLt GEMM with the bias and residual in its
- * epilogue, asynchronous on `stream`. The first call on a device creates a
- * cuBLASLt handle and a 32 MiB workspace that the library keeps.
+ * epilogue (bf16 output with a bias: the product goes to an fp32 buffer and
+ * one kernel adds bias and residual, so the output is rounded once),
+ * asynchronous on `stream`. The first call on a device creates a cuBLASLt
+ * handle and a 32 MiB workspace that the library keeps (and the fp32
+ * buffer, grown on demand).
  */
 int ca_linear(const ca_linear_args* a, void* stream);
 
