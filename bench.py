@@ -554,8 +554,8 @@ def run_extras(dev, peaks, scratch):
     rb = pj.row_bytes(pj.Q4_K, cols)
     wq = rng.integers(0, 256, (rows, rb), dtype=np.uint8)
     blk = wq.reshape(-1, 144)
-    blk[:, 0:2] = np.float16(0.01).view(np.uint8)  # moderate d / dmin in every block
-    blk[:, 2:4] = np.float16(0.005).view(np.uint8)
+    blk[:, 0:2] = np.array([0.01], np.float16).view(np.uint8)  # moderate d / dmin in every block
+    blk[:, 2:4] = np.array([0.005], np.float16).view(np.uint8)
     src = torch.from_numpy(wq).to(dev)
     w = torch.empty(rows, cols, dtype=torch.bfloat16, device=dev)
     ms = _event_ms(lambda: pj.dequantize(pj.Q4_K, src, rows, cols, w), 20, scratch)
@@ -829,7 +829,10 @@ def run_ours(args, cfg):
     # per-candidate statistics (HBM).
     extras = None
     if world == 1 and not args.no_by_config:
-        extras = run_extras(dev, peaks, scratch)
+        try:
+            extras = run_extras(dev, peaks, scratch)
+        except Exception as e:  # an optional leg must not lose the main line
+            extras = {"error": f"{type(e).__name__}: {e}"}
 
     # Head sharding (N > 1): every rank computes its kv-head slice (and the
     # query heads of those groups) of ONE global batch of the config, then
