@@ -897,6 +897,8 @@ int ca_dequantize(int32_t qtype, const void* src, int64_t rows, int64_t cols,
   const int64_t ds = dst_stride ? dst_stride : cols;
   if (ds < cols || ds % 8 || (reinterpret_cast<uintptr_t>(dst) & 15u)) return CA_ERR_INVALID;
   if (!row_ids && n_out > rows) return CA_ERR_INVALID;
+  // Q4_K blocks are read with 32- and 64-bit loads.
+  if (qtype == kQ4_K && (reinterpret_cast<uintptr_t>(src) & 7u)) return CA_ERR_INVALID;
   if (n_out == 0) return CA_OK;
   DequantParams p{};
   p.src = static_cast<const uint8_t*>(src);

@@ -55,14 +55,27 @@ __device__ __forceinline__ int q4k_scale(const uint8_t* s, int j, int which) {
 // Eight consecutive weights idx .. idx + 7 (idx % 8 == 0) of one row.
 __device__ __forceinline__ void dequant8(int qtype, const uint8_t* row, int idx, float (&o)[8]) {
   if (qtype == kQ4_K) {
+    // Blocks of 144 bytes keep 8-byte alignment: the header (d, dmin) and
+    // the 12 scale bytes load as 32-bit words, the lane's 8 quant bytes as
+    // one 64-bit word.
     const uint8_t* b = row + (idx >> 8) * 144;
     const int v = idx & 255;
     const int pair = v >> 6, w = v & 63;  // 64 weights share one byte range
     const int sub = 2 * pair + (w >= 32 ? 1 : 0);
-    const float d = h2f(b), dmin = h2f(b + 2);
-    const float sc = static_cast<float>(q4k_scale(b + 4, sub, 0));
-    const float mn = static_cast<float>(q4k_scale(b + 4, sub, 1));
-    const uint8_t* qs = b + 16 + pair * 32 + (w & 31);
+    const uint32_t hdr = __ldg(reinterpret_cast<const uint32_t*>(b));
+    const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr & 0xffffu)));
+    const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr >> 16)));
+    uint8_t s12[12];
+    *reinterpret_cast<uint32_t*>(s12) = __ldg(reinterpret_cast<const uint32_t*>(b + 4));
+    *reinterpret_cast<uint32_t*>(s12 + 4) = __ldg(reinterpret_cast<const uint32_t*>(b + 8));
+    *reinterpret_cast<uint32_t*>(s12 + 8) = __ldg(reinterpret_cast<const uint32_t*>(b + 12));
+    const float sc = static_cast<float>(q4k_scale(s12, sub, 0));
+    const float mn = static_cast<float>(q4k_scale(s12, sub, 1));
+    const uint2 qv = __ldg(reinterpret_cast<const uint2*>(b + 16 + pair * 32 + (w & 31)));
+    const uint8_t qs[8] = {static_cast<uint8_t>(qv.x), static_cast<uint8_t>(qv.x >> 8),
+                           static_cast<uint8_t>(qv.x >> 16), static_cast<uint8_t>(qv.x >> 24),
+                           static_cast<uint8_t>(qv.y), static_cast<uint8_t>(qv.y >> 8),
+                           static_cast<uint8_t>(qv.y >> 16), static_cast<uint8_t>(qv.y >> 24)};
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int q = w >= 32 ? (qs[k] >> 4) : (qs[k] & 0xF);

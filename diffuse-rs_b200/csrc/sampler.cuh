@@ -9,9 +9,12 @@
 //   entropy  compute_entropy (:7-20): sum of -p * lp over entries with
 //            p > 1e-10, lp = (l - max) - ln(sum exp(l - max))
 //   prob     exp(top1 - log_sum_exp(row)) (:22-25)
+// Exponentials use the fast exp (ex2.approx; relative error ~1e-6 for the
+// arguments here), well inside the step's tolerance on entropy and prob.
 // The logits are read from HBM once per row for the first four reductions
-// (an online max / sum of exponentials) and a second time, from L2 while the
-// wave's rows are resident, for the entropy's thresholded sum. HBM-bound.
+// (an online max / sum of exponentials) and a second time, mostly from L2
+// (the resident CTAs' rows, 0.5 MB each at a 126k vocabulary), for the
+// entropy's thresholded sum. HBM-bound.
 #pragma once
 
 #include <cstdint>
@@ -47,13 +50,13 @@ struct CandAcc {
 
 __device__ __forceinline__ void cand_push(CandAcc& a, float x, int j) {
   if (x > a.t1) {
-    a.s = (a.t1 == -INFINITY ? 0.f : a.s * expf(a.t1 - x)) + 1.f;
+    a.s = (a.t1 == -INFINITY ? 0.f : a.s * __expf(a.t1 - x)) + 1.f;
     a.t2 = a.t1;
     a.t1 = x;
     a.idx = j;
   } else {
     if (x > a.t2) a.t2 = x;
-    if (x != -INFINITY) a.s += expf(x - a.t1);
+    if (x != -INFINITY) a.s += __expf(x - a.t1);
   }
 }
 
@@ -101,10 +104,27 @@ __global__ void __launch_bounds__(kCandThreads) cand_stats_kernel(const CandPara
   const bool vec = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
   long long done = 0;
   if (vec) {
+    // Four 16-byte loads in flight per thread before any is consumed: one
+    // CTA per row leaves few warps per SM, so each must keep HBM busy.
     const long long n4 = n / 4;
     const float4* r4 = reinterpret_cast<const float4*>(row);
-    for (long long i = tid; i < n4; i += kCandThreads) {
-      const float4 v = __ldcs(r4 + i);  // streamed: the entropy pass rereads from L2
+    constexpr int U = 4;
+    long long i = tid;
+    for (; i + (U - 1) * kCandThreads < n4; i += U * kCandThreads) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = __ldg(r4 + i + u * kCandThreads);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = static_cast<int>(4 * (i + u * kCandThreads));
+        cand_push(a, v[u].x, j);
+        cand_push(a, v[u].y, j + 1);
+        cand_push(a, v[u].z, j + 2);
+        cand_push(a, v[u].w, j + 3);
+      }
+    }
+    for (; i < n4; i += kCandThreads) {
+      const float4 v = __ldg(r4 + i);
       const int j = static_cast<int>(4 * i);
       cand_push(a, v.x, j);
       cand_push(a, v.y, j + 1);
@@ -134,14 +154,28 @@ __global__ void __launch_bounds__(kCandThreads) cand_stats_kernel(const CandPara
     // acc - p * lp over entries with p = exp(lp) > 1e-10 (compute_entropy).
     auto term = [&](float x) {
       const float lp = (x - mx) - log_sum;
-      const float pr = expf(lp);
+      const float pr = __expf(lp);
       if (pr > 1e-10f) h -= pr * lp;
     };
     if (vec) {
       const long long n4 = n / 4;
       const float4* r4 = reinterpret_cast<const float4*>(row);
-      for (long long i = tid; i < n4; i += kCandThreads) {
-        const float4 v = r4[i];
+      constexpr int U = 4;
+      long long i = tid;
+      for (; i + (U - 1) * kCandThreads < n4; i += U * kCandThreads) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = __ldg(r4 + i + u * kCandThreads);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          term(v[u].x);
+          term(v[u].y);
+          term(v[u].z);
+          term(v[u].w);
+        }
+      }
+      for (; i < n4; i += kCandThreads) {
+        const float4 v = __ldg(r4 + i);
         term(v.x);
         term(v.y);
         term(v.z);

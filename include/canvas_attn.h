@@ -319,7 +319,7 @@ int64_t ca_tokens_to_unmask(int64_t step, int64_t total_steps, int64_t masked,
  * embedding gather of embed_tokens, src/model/forward.rs:175-246), or row i
  * when row_ids is NULL, times `scale` (1 = none; Gemma's embed_scale).
  * dst: 16-byte aligned, row stride dst_stride elements (0 = cols, a
- * multiple of 8). cols must be a multiple of 256 (Q4_K, Q6_K), 32 (Q4_0,
+ * multiple of 8); Q4_K sources 8-byte aligned. cols must be a multiple of 256 (Q4_K, Q6_K), 32 (Q4_0,
  * Q8_0) or 8 (F16). A row id out of range skips that row and sets *status
  * (device int32, may be NULL) to 1.
  */
