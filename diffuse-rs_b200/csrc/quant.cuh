@@ -116,41 +116,64 @@ __device__ __forceinline__ void dequant8(int qtype, const uint8_t* row, int idx,
   }
 }
 
-// One warp per 256 output weights of one output row (grid-stride).
+// One warp per 256 output weights of one output row, four units per warp
+// iteration (grid-stride): the loads of all four are issued before any is
+// consumed, so each warp keeps several block reads in flight.
+__device__ __forceinline__ void dequant_store(const DequantParams& p, long long i, int idx,
+                                              float (&o)[8]) {
+  if (p.scale != 1.f) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(o[k], p.scale);
+  }
+  const long long off = i * p.dst_stride + idx;
+  if (p.dst_f32) {
+    float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.dst) + off);
+    d[0] = make_float4(o[0], o[1], o[2], o[3]);
+    d[1] = make_float4(o[4], o[5], o[6], o[7]);
+  } else {
+    uint4 w;
+    w.x = pack_bf16(o[0], o[1]);
+    w.y = pack_bf16(o[2], o[3]);
+    w.z = pack_bf16(o[4], o[5]);
+    w.w = pack_bf16(o[6], o[7]);
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.dst) + off) = w;
+  }
+}
+
 __global__ void __launch_bounds__(256) dequant_kernel(const DequantParams p) {
+  constexpr int U = 4;
   const int lane = threadIdx.x & 31;
   const long long units_per_row = (p.cols + 255) / 256;
   const long long units = p.n_out * units_per_row;
   const long long rb = qrow_bytes(p.qtype, p.cols);
-  for (long long u = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-       u < units; u += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
-    const long long i = u / units_per_row;
-    const int idx = static_cast<int>((u % units_per_row) * 256 + lane * 8);
-    if (idx >= p.cols) continue;
-    const long long r = p.row_ids ? p.row_ids[i] : i;
-    if (r < 0 || r >= p.rows) {
-      if (lane == 0 && p.err) atomicExch(p.err, 1);
-      continue;
-    }
-    float o[8];
-    dequant8(p.qtype, p.src + r * rb, idx, o);
-    if (p.scale != 1.f) {
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long u0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       u0 < units; u0 += U * nwarps) {
+    float o[U][8];
+    long long oi[U];
+    int oidx[U];
+    bool ok[U];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(o[k], p.scale);
+    for (int k = 0; k < U; ++k) {
+      const long long u = u0 + k * nwarps;
+      ok[k] = false;
+      if (u >= units) continue;
+      const long long i = u / units_per_row;
+      const int idx = static_cast<int>((u % units_per_row) * 256 + lane * 8);
+      if (idx >= p.cols) continue;
+      const long long r = p.row_ids ? p.row_ids[i] : i;
+      if (r < 0 || r >= p.rows) {
+        if (lane == 0 && p.err) atomicExch(p.err, 1);
+        continue;
+      }
+      dequant8(p.qtype, p.src + r * rb, idx, o[k]);
+      oi[k] = i;
+      oidx[k] = idx;
+      ok[k] = true;
     }
-    const long long off = i * p.dst_stride + idx;
-    if (p.dst_f32) {
-      float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.dst) + off);
-      d[0] = make_float4(o[0], o[1], o[2], o[3]);
-      d[1] = make_float4(o[4], o[5], o[6], o[7]);
-    } else {
-      uint4 w;
-      w.x = pack_bf16(o[0], o[1]);
-      w.y = pack_bf16(o[2], o[3]);
-      w.z = pack_bf16(o[4], o[5]);
-      w.w = pack_bf16(o[6], o[7]);
-      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.dst) + off) = w;
-    }
+#pragma unroll
+    for (int k = 0; k < U; ++k)
+      if (ok[k]) dequant_store(p, oi[k], oidx[k], o[k]);
   }
 }
 
