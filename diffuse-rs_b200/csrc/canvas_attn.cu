@@ -857,7 +857,8 @@ int ca_candidate_stats(const ca_cand_args* a, void* stream) {
   p.entropy = a->entropy;
   p.margin = a->margin;
   p.prob = a->prob;
-  ca::cand_stats_kernel<<<a->n_cand, ca::kCandThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  const int grid = std::min(a->n_cand, 148);
+  ca::cand_stats_kernel<<<grid, ca::kCandThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
 }
 
@@ -912,8 +913,8 @@ int ca_dequantize(int32_t qtype, const void* src, int64_t rows, int64_t cols,
   p.scale = scale;
   p.qtype = qtype;
   p.err = status;
-  const long long warps = (n_out * ((cols + 255) / 256) + 3) / 4;  // four units per warp
-  const int blocks = static_cast<int>(std::min<long long>((warps + 7) / 8, 148LL * 8));
+  const long long warps = n_out * ((cols + 255) / 256);
+  const int blocks = static_cast<int>(std::min<long long>((warps + 7) / 8, 148LL * 16));
   dequant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
 }

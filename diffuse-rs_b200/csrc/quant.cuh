@@ -45,6 +45,13 @@ __device__ __forceinline__ float h2f(const uint8_t* p) {
   return __half2float(__ushort_as_half(h));  // exact, subnormals included
 }
 
+// Exact float of a small integer (|v| < 2^22) without the XU pipe's
+// int-to-float conversion: v is added to the mantissa of 1.5 * 2^23 and that
+// constant subtracted again (both steps exact).
+__device__ __forceinline__ float small_i2f(int v) {
+  return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f);
+}
+
 // The 6-bit scale (which = 0) or min (which = 1) of sub-block j of a Q4_K
 // block, from its 12 packed bytes (the utmp unpacking of the reference).
 __device__ __forceinline__ int q4k_scale(const uint8_t* s, int j, int which) {
@@ -69,8 +76,8 @@ __device__ __forceinline__ void dequant8(int qtype, const uint8_t* row, int idx,
     *reinterpret_cast<uint32_t*>(s12) = __ldg(reinterpret_cast<const uint32_t*>(b + 4));
     *reinterpret_cast<uint32_t*>(s12 + 4) = __ldg(reinterpret_cast<const uint32_t*>(b + 8));
     *reinterpret_cast<uint32_t*>(s12 + 8) = __ldg(reinterpret_cast<const uint32_t*>(b + 12));
-    const float sc = static_cast<float>(q4k_scale(s12, sub, 0));
-    const float mn = static_cast<float>(q4k_scale(s12, sub, 1));
+    const float sc = small_i2f(q4k_scale(s12, sub, 0));
+    const float mn = small_i2f(q4k_scale(s12, sub, 1));
     const uint2 qv = __ldg(reinterpret_cast<const uint2*>(b + 16 + pair * 32 + (w & 31)));
     const uint8_t qs[8] = {static_cast<uint8_t>(qv.x), static_cast<uint8_t>(qv.x >> 8),
                            static_cast<uint8_t>(qv.x >> 16), static_cast<uint8_t>(qv.x >> 24),
@@ -80,7 +87,7 @@ __device__ __forceinline__ void dequant8(int qtype, const uint8_t* row, int idx,
     for (int k = 0; k < 8; ++k) {
       const int q = w >= 32 ? (qs[k] >> 4) : (qs[k] & 0xF);
       // d * sc * q - dmin * mn, left to right, no contraction
-      o[k] = __fsub_rn(__fmul_rn(__fmul_rn(d, sc), static_cast<float>(q)), __fmul_rn(dmin, mn));
+      o[k] = __fsub_rn(__fmul_rn(__fmul_rn(d, sc), small_i2f(q)), __fmul_rn(dmin, mn));
     }
   } else if (qtype == kQ6_K) {
     const uint8_t* b = row + (idx >> 8) * 210;
@@ -88,12 +95,12 @@ __device__ __forceinline__ void dequant8(int qtype, const uint8_t* row, int idx,
     const int h = v >> 7, g = (v & 127) >> 5, l0 = v & 31;
     const uint8_t* ql = b + h * 64 + (g & 1) * 32 + l0;
     const uint8_t* qh = b + 128 + h * 32 + l0;
-    const float sc = __fmul_rn(h2f(b + 208), static_cast<float>(static_cast<int8_t>(b[192 + (v >> 4)])));
+    const float sc = __fmul_rn(h2f(b + 208), small_i2f(static_cast<int8_t>(b[192 + (v >> 4)])));
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int lo = g < 2 ? (ql[k] & 0xF) : (ql[k] >> 4);
       const int hi = (qh[k] >> (2 * g)) & 3;
-      o[k] = __fmul_rn(sc, static_cast<float>((lo | (hi << 4)) - 32));
+      o[k] = __fmul_rn(sc, small_i2f((lo | (hi << 4)) - 32));
     }
   } else if (qtype == kQ4_0) {
     const uint8_t* b = row + (idx >> 5) * 18;
@@ -102,78 +109,55 @@ __device__ __forceinline__ void dequant8(int qtype, const uint8_t* row, int idx,
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int q = w < 16 ? (b[2 + w + k] & 0xF) : (b[2 + w - 16 + k] >> 4);
-      o[k] = __fmul_rn(d, __fsub_rn(static_cast<float>(q), 8.0f));
+      o[k] = __fmul_rn(d, __fsub_rn(small_i2f(q), 8.0f));
     }
   } else if (qtype == kQ8_0) {
     const uint8_t* b = row + (idx >> 5) * 34;
     const float d = h2f(b);
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      o[k] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(b[2 + (idx & 31) + k])));
+      o[k] = __fmul_rn(d, small_i2f(static_cast<int8_t>(b[2 + (idx & 31) + k])));
   } else {  // F16
 #pragma unroll
     for (int k = 0; k < 8; ++k) o[k] = h2f(row + 2 * (idx + k));
   }
 }
 
-// One warp per 256 output weights of one output row, four units per warp
-// iteration (grid-stride): the loads of all four are issued before any is
-// consumed, so each warp keeps several block reads in flight.
-__device__ __forceinline__ void dequant_store(const DequantParams& p, long long i, int idx,
-                                              float (&o)[8]) {
-  if (p.scale != 1.f) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(o[k], p.scale);
-  }
-  const long long off = i * p.dst_stride + idx;
-  if (p.dst_f32) {
-    float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.dst) + off);
-    d[0] = make_float4(o[0], o[1], o[2], o[3]);
-    d[1] = make_float4(o[4], o[5], o[6], o[7]);
-  } else {
-    uint4 w;
-    w.x = pack_bf16(o[0], o[1]);
-    w.y = pack_bf16(o[2], o[3]);
-    w.z = pack_bf16(o[4], o[5]);
-    w.w = pack_bf16(o[6], o[7]);
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.dst) + off) = w;
-  }
-}
-
-__global__ void __launch_bounds__(256) dequant_kernel(const DequantParams p) {
-  constexpr int U = 4;
+// One warp per 256 output weights of one output row (grid-stride).
+__global__ void __launch_bounds__(256, 4) dequant_kernel(const DequantParams p) {
   const int lane = threadIdx.x & 31;
   const long long units_per_row = (p.cols + 255) / 256;
   const long long units = p.n_out * units_per_row;
   const long long rb = qrow_bytes(p.qtype, p.cols);
-  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
-  for (long long u0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-       u0 < units; u0 += U * nwarps) {
-    float o[U][8];
-    long long oi[U];
-    int oidx[U];
-    bool ok[U];
-#pragma unroll
-    for (int k = 0; k < U; ++k) {
-      const long long u = u0 + k * nwarps;
-      ok[k] = false;
-      if (u >= units) continue;
-      const long long i = u / units_per_row;
-      const int idx = static_cast<int>((u % units_per_row) * 256 + lane * 8);
-      if (idx >= p.cols) continue;
-      const long long r = p.row_ids ? p.row_ids[i] : i;
-      if (r < 0 || r >= p.rows) {
-        if (lane == 0 && p.err) atomicExch(p.err, 1);
-        continue;
-      }
-      dequant8(p.qtype, p.src + r * rb, idx, o[k]);
-      oi[k] = i;
-      oidx[k] = idx;
-      ok[k] = true;
+  for (long long u = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       u < units; u += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const long long i = u / units_per_row;
+    const int idx = static_cast<int>((u % units_per_row) * 256 + lane * 8);
+    if (idx >= p.cols) continue;
+    const long long r = p.row_ids ? p.row_ids[i] : i;
+    if (r < 0 || r >= p.rows) {
+      if (lane == 0 && p.err) atomicExch(p.err, 1);
+      continue;
     }
+    float o[8];
+    dequant8(p.qtype, p.src + r * rb, idx, o);
+    if (p.scale != 1.f) {
 #pragma unroll
-    for (int k = 0; k < U; ++k)
-      if (ok[k]) dequant_store(p, oi[k], oidx[k], o[k]);
+      for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(o[k], p.scale);
+    }
+    const long long off = i * p.dst_stride + idx;
+    if (p.dst_f32) {
+      float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.dst) + off);
+      d[0] = make_float4(o[0], o[1], o[2], o[3]);
+      d[1] = make_float4(o[4], o[5], o[6], o[7]);
+    } else {
+      uint4 w;
+      w.x = pack_bf16(o[0], o[1]);
+      w.y = pack_bf16(o[2], o[3]);
+      w.z = pack_bf16(o[4], o[5]);
+      w.w = pack_bf16(o[6], o[7]);
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.dst) + off) = w;
+    }
   }
 }
 
