@@ -913,8 +913,9 @@ int ca_dequantize(int32_t qtype, const void* src, int64_t rows, int64_t cols,
   p.scale = scale;
   p.qtype = qtype;
   p.err = status;
-  const long long warps = n_out * ((cols + 255) / 256);
-  const int blocks = static_cast<int>(std::min<long long>((warps + 7) / 8, 148LL * 16));
+  const long long items = n_out * (((cols + 255) / 256 + kUnits - 1) / kUnits);
+  if (items > UINT_MAX / 2) return CA_ERR_UNSUPPORTED;  // 32-bit work-item indices
+  const int blocks = static_cast<int>(std::min<long long>((items + 7) / 8, 148LL * 16));
   dequant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
 }

@@ -123,40 +123,59 @@ __device__ __forceinline__ void dequant8(int qtype, const uint8_t* row, int idx,
   }
 }
 
-// One warp per 256 output weights of one output row (grid-stride).
-__global__ void __launch_bounds__(256, 4) dequant_kernel(const DequantParams p) {
+// A work item is kUnits consecutive 256-weight units of one output row; one
+// warp per item (grid-stride), all loads of the item issued before any is
+// consumed. Item indices are 32-bit: one unsigned division per item.
+constexpr int kUnits = 4;
+
+__device__ __forceinline__ void dequant_store(const DequantParams& p, long long i, int idx,
+                                              const float (&o)[8]) {
+  const long long off = i * p.dst_stride + idx;
+  if (p.dst_f32) {
+    float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.dst) + off);
+    d[0] = make_float4(o[0], o[1], o[2], o[3]);
+    d[1] = make_float4(o[4], o[5], o[6], o[7]);
+  } else {
+    uint4 w;
+    w.x = pack_bf16(o[0], o[1]);
+    w.y = pack_bf16(o[2], o[3]);
+    w.z = pack_bf16(o[4], o[5]);
+    w.w = pack_bf16(o[6], o[7]);
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.dst) + off) = w;
+  }
+}
+
+__global__ void __launch_bounds__(256) dequant_kernel(const DequantParams p) {
   const int lane = threadIdx.x & 31;
-  const long long units_per_row = (p.cols + 255) / 256;
-  const long long units = p.n_out * units_per_row;
+  const unsigned units_per_row = static_cast<unsigned>((p.cols + 255) / 256);
+  const unsigned items_per_row = (units_per_row + kUnits - 1) / kUnits;
+  const unsigned items = static_cast<unsigned>(p.n_out) * items_per_row;
   const long long rb = qrow_bytes(p.qtype, p.cols);
-  for (long long u = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-       u < units; u += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
-    const long long i = u / units_per_row;
-    const int idx = static_cast<int>((u % units_per_row) * 256 + lane * 8);
-    if (idx >= p.cols) continue;
+  const unsigned nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (unsigned it = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; it < items; it += nwarps) {
+    const unsigned i = it / items_per_row;
+    const unsigned u0 = (it - i * items_per_row) * kUnits;
     const long long r = p.row_ids ? p.row_ids[i] : i;
     if (r < 0 || r >= p.rows) {
       if (lane == 0 && p.err) atomicExch(p.err, 1);
       continue;
     }
-    float o[8];
-    dequant8(p.qtype, p.src + r * rb, idx, o);
-    if (p.scale != 1.f) {
+    const uint8_t* row = p.src + r * rb;
+    float o[kUnits][8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(o[k], p.scale);
+    for (int k = 0; k < kUnits; ++k) {
+      const int idx = static_cast<int>((u0 + k) * 256 + lane * 8);
+      if (idx < p.cols) dequant8(p.qtype, row, idx, o[k]);
     }
-    const long long off = i * p.dst_stride + idx;
-    if (p.dst_f32) {
-      float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.dst) + off);
-      d[0] = make_float4(o[0], o[1], o[2], o[3]);
-      d[1] = make_float4(o[4], o[5], o[6], o[7]);
-    } else {
-      uint4 w;
-      w.x = pack_bf16(o[0], o[1]);
-      w.y = pack_bf16(o[2], o[3]);
-      w.z = pack_bf16(o[4], o[5]);
-      w.w = pack_bf16(o[6], o[7]);
-      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.dst) + off) = w;
+#pragma unroll
+    for (int k = 0; k < kUnits; ++k) {
+      const int idx = static_cast<int>((u0 + k) * 256 + lane * 8);
+      if (idx >= p.cols) break;
+      if (p.scale != 1.f) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[k][e] = __fmul_rn(o[k][e], p.scale);
+      }
+      dequant_store(p, i, idx, o[k]);
     }
   }
 }
