@@ -158,6 +158,9 @@ int clamp_opt(int64_t v) {  // Option<usize> as int32 (None = -1)
 #ifndef CA_FUSE_Q
 #define CA_FUSE_Q 1
 #endif
+#ifndef CA_PREP_BULK
+#define CA_PREP_BULK 1
+#endif
 struct QFuse {
   const float* w;     // q norm gains [128] or null
   const float* rope;  // [rope_len, 64, 2] (sin, cos)
@@ -354,7 +357,36 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   const long long toks =
       varlen ? a->total_active : static_cast<long long>(a->batch) * a->n_active;
   const long long jobs = toks * (Hp + 2 * Hkv);
-  if (vec && (hd == 64 || hd == 128 || hd == 256)) {
+  pp.err = a->status;
+  const long long stage = static_cast<long long>(Hp + 2 * Hkv) * hd * 2;
+  const size_t bulk_smem = kPrepStages * stage + 16 * kPrepStages;
+  if (CA_PREP_BULK && vec && (hd == 64 || hd == 128 || hd == 256) && bulk_smem <= 112 * 1024) {
+    // Bulk-copy pre-ops: a shared-memory ring per CTA, several CTAs per SM.
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
+    static bool attr_done[3][kMaxDevices] = {};
+    const int ti = hd == 64 ? 0 : hd == 128 ? 1 : 2;
+    const void* fn = hd == 64 ? reinterpret_cast<const void*>(prep_bulk_kernel<8>)
+                     : hd == 128 ? reinterpret_cast<const void*>(prep_bulk_kernel<16>)
+                                 : reinterpret_cast<const void*>(prep_bulk_kernel<32>);
+    if (!attr_done[ti][dev]) {
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024) !=
+          cudaSuccess)
+        return CA_ERR_CUDA;
+      attr_done[ti][dev] = true;
+    }
+    // Exactly one wave of resident CTAs (they stride over the tokens).
+    int per_sm = 1, n_sm = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kPrepThreads, bulk_smem) !=
+            cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const int blocks = static_cast<int>(std::min<long long>(toks, 1LL * n_sm * per_sm));
+    if (hd == 64) prep_bulk_kernel<8><<<blocks, kPrepThreads, bulk_smem, st>>>(pp);
+    else if (hd == 128) prep_bulk_kernel<16><<<blocks, kPrepThreads, bulk_smem, st>>>(pp);
+    else prep_bulk_kernel<32><<<blocks, kPrepThreads, bulk_smem, st>>>(pp);
+  } else if (vec && (hd == 64 || hd == 128 || hd == 256)) {
     // 16-row jobs unless that leaves fewer jobs than 64 warps per SM; then
     // one warp step per job (256 / head_dim rows).
     pp.rows_per_job = 16;

@@ -13,6 +13,8 @@
 #include <cstdint>
 #include <cuda_bf16.h>
 
+#include "sm100.cuh"
+
 namespace ca {
 
 struct PrepParams {
@@ -40,6 +42,7 @@ struct PrepParams {
   const int* cu_active;
   const int* cu_total;
   long long total_active;
+  int* err;  // status word of the call (null: the device-wide word)
 };
 
 // Active tokens of the whole call.
@@ -392,6 +395,190 @@ __global__ void __launch_bounds__(256) prep_pair_kernel(const PrepParams p) {
     }
   }
 }
+
+// Bulk-copy form (head_dim 64 / 128 / 256, rope_dim % 16 == 0, 16-byte
+// aligned Q/K/V): one producer lane per CTA streams each token's Q, K and V
+// rows (contiguous in the inputs: H, Hkv and Hkv rows of head_dim) into a
+// ring of kPrepStages shared-memory stages with cp.async.bulk, so many
+// bytes are in flight per SM without holding registers; eight consumer warps
+// normalise and rotate the rows out of shared memory (a NeoX partner element
+// sits in the same staged row, so no exchange is needed) and store them to
+// q_work and the cache. Arithmetic identical to prep_token_kernel.
+constexpr int kPrepStages = 4;
+constexpr int kPrepConsumers = 8;  // warps
+constexpr int kPrepThreads = 32 * (kPrepConsumers + 1);
+
+template <int LPR>
+__global__ void __launch_bounds__(kPrepThreads) prep_bulk_kernel(const PrepParams p) {
+  constexpr int RPW = 32 / LPR;  // rows per warp per step
+  constexpr int HD = LPR * 8;
+  extern __shared__ __align__(128) uint8_t prep_ring[];
+  const int rows = p.H + 2 * p.Hkv;
+  const uint32_t stage_bytes = static_cast<uint32_t>(rows) * HD * 2;
+  const uint32_t ring = smem_u32(prep_ring);
+  const uint32_t bars = ring + kPrepStages * stage_bytes;  // full[S], empty[S]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long n_tok = prep_tokens(p);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPrepStages; ++s) {
+      mbar_init(bars + 8 * s, 1);
+      mbar_init(bars + 8 * (kPrepStages + s), kPrepConsumers);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  bool dead = false;
+  if (warp == kPrepConsumers) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int it = 0;
+      for (long long tok = blockIdx.x; tok < n_tok; tok += gridDim.x, ++it) {
+        const int s = it % kPrepStages;
+        if (it >= kPrepStages &&
+            !mbar_wait(bars + 8 * (kPrepStages + s), ((it / kPrepStages) - 1) & 1, dead, p.err))
+          break;
+        const uint32_t dst = ring + s * stage_bytes;
+        mbar_arrive_expect_tx(bars + 8 * s, stage_bytes);
+        if (p.H > 0) bulk_load(dst, p.q + tok * p.H * HD, p.H * HD * 2, bars + 8 * s);
+        bulk_load(dst + p.H * HD * 2, p.k + tok * p.Hkv * HD, p.Hkv * HD * 2, bars + 8 * s);
+        bulk_load(dst + (p.H + p.Hkv) * HD * 2, p.v + tok * p.Hkv * HD, p.Hkv * HD * 2,
+                  bars + 8 * s);
+      }
+      // Leave no bulk copy in flight: wait (bounded) for the last stages.
+      bool d2 = false;
+      for (int j = it > kPrepStages ? it - kPrepStages : 0; j < it; ++j)
+        mbar_wait(bars + 8 * (j % kPrepStages), (j / kPrepStages) & 1, d2, p.err);
+    }
+    return;
+  }
+  // ------------------------------------------------------------ consumers
+  const int sub = lane / LPR, sl = lane % LPR;
+  const int e0 = sl * 8;
+  const int half = p.rope_dim / 2;
+  const bool rot = e0 < 2 * half;
+  const int pe = e0 < half ? e0 + half : e0 - half;  // NeoX partner elements
+  int it = 0;
+  for (long long tok = blockIdx.x; tok < n_tok; tok += gridDim.x, ++it) {
+    const int s = it % kPrepStages;
+    if (!mbar_wait(bars + 8 * s, (it / kPrepStages) & 1, dead, p.err)) break;
+    const uint8_t* stage = prep_ring + s * stage_bytes;
+    const int pos = __ldg(p.pos + tok);
+    const long long crow = cache_row(p, tok, pos);
+    float sn[8], cs[8];
+    {
+      const int idx = e0 < half ? e0 : e0 - half;
+      const float4* t4 =
+          reinterpret_cast<const float4*>(p.rope + 2 * (static_cast<long long>(pos) * half + idx));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = rot ? __ldg(t4 + i) : make_float4(0.f, 1.f, 0.f, 1.f);
+        sn[2 * i] = v.x;
+        cs[2 * i] = v.y;
+        sn[2 * i + 1] = v.z;
+        cs[2 * i + 1] = v.w;
+      }
+    }
+    for (int r0 = warp * RPW; r0 < rows; r0 += kPrepConsumers * RPW) {
+      const int r = r0 + sub;
+      const bool active = r < rows;
+      const int rr = active ? r : r0;
+      __nv_bfloat16* dst;
+      const float* w = nullptr;
+      bool norm, rope = true;
+      if (rr < p.H) {
+        dst = p.q_out + (tok * p.H + rr) * HD;
+        w = p.q_norm_w;
+        norm = w != nullptr;
+      } else if (rr < p.H + p.Hkv) {
+        dst = p.cache_k + (crow * p.Hkv + (rr - p.H)) * HD;
+        w = p.k_norm_w;
+        norm = w != nullptr;
+      } else {
+        dst = p.cache_v + (crow * p.Hkv + (rr - p.H - p.Hkv)) * HD;
+        norm = p.v_norm != 0;
+        rope = false;  // V is not rotated (forward.rs:310 rotates Q and K only)
+      }
+      const uint8_t* src = stage + static_cast<size_t>(rr) * HD * 2;
+      float x[8], xp[8];
+      {
+        const uint4 raw = *reinterpret_cast<const uint4*>(src + e0 * 2);
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x[2 * i] = __uint_as_float(wv[i] << 16);
+          x[2 * i + 1] = __uint_as_float(wv[i] & 0xffff0000u);
+        }
+      }
+      const bool do_rot = rope && rot;
+      if (do_rot) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(src + pe * 2);
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xp[2 * i] = __uint_as_float(wv[i] << 16);
+          xp[2 * i + 1] = __uint_as_float(wv[i] & 0xffff0000u);
+        }
+      }
+      // Every lane joins the reduction; `norm` may differ between the rows.
+      double ss = 0.0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += static_cast<double>(__fmul_rn(x[i], x[i]));
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (norm) {
+        const float sc =
+            __fdiv_rn(1.f, static_cast<float>(sqrt(ss / HD + static_cast<double>(p.eps))));
+        if (w) {
+          const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + e0));
+          const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + e0) + 1);
+          const float wf[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], sc), wf[i]);
+          if (do_rot) {
+            const float4 q0 = __ldg(reinterpret_cast<const float4*>(w + pe));
+            const float4 q1 = __ldg(reinterpret_cast<const float4*>(w + pe) + 1);
+            const float wp[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xp[i] = __fmul_rn(__fmul_rn(xp[i], sc), wp[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] = __fmul_rn(x[i], sc);
+          if (do_rot) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xp[i] = __fmul_rn(xp[i], sc);
+          }
+        }
+      }
+      float y[8];
+      if (do_rot) {
+        if (e0 < half) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            y[i] = __fsub_rn(__fmul_rn(x[i], cs[i]), __fmul_rn(xp[i], sn[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            y[i] = __fadd_rn(__fmul_rn(xp[i], sn[i]), __fmul_rn(x[i], cs[i]));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = x[i];
+      }
+      if (active) {
+        uint4 o;
+        o.x = pack2_bf16(y[0], y[1]);
+        o.y = pack2_bf16(y[2], y[3]);
+        o.z = pack2_bf16(y[4], y[5]);
+        o.w = pack2_bf16(y[6], y[7]);
+        *reinterpret_cast<uint4*>(dst + e0) = o;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars + 8 * (kPrepStages + s));
+  }
+}
+
 
 // fp32 -> bf16 (round to nearest even), used by the host-buffer entry point.
 __global__ void f32_to_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out,

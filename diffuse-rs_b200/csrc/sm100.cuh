@@ -121,6 +121,18 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// Contiguous bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory, completing on
+// the mbarrier `bar`. Plain per-CTA copy.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // 4-D tiled bulk tensor store from this CTA's shared memory (bulk group).
 __device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int32_t x, int32_t y,
                                              int32_t z, int32_t w) {
