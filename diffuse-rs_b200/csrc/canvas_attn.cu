@@ -360,8 +360,12 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   pp.err = a->status;
   const long long stage = static_cast<long long>(Hp + 2 * Hkv) * hd * 2;
   const size_t bulk_smem = kPrepStages * stage + 16 * kPrepStages;
-  if (CA_PREP_BULK && vec && (hd == 64 || hd == 128 || hd == 256) && bulk_smem <= 112 * 1024) {
-    // Bulk-copy pre-ops: a shared-memory ring per CTA, several CTAs per SM.
+  // Bulk-copy pre-ops (a shared-memory ring per CTA) at head_dim 256: c5's
+  // layer block 4.59 ms against 4.75 with prep_pair_kernel. At head_dim 128
+  // both forms are bound by the per-row arithmetic (f64 sum of squares,
+  // shuffles), not by bytes in flight, and the token kernel measured 1.6%
+  // faster (c3 block 1.345 vs 1.366 ms).
+  if (CA_PREP_BULK && vec && hd == 256 && bulk_smem <= 112 * 1024) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
     static bool attr_done[3][kMaxDevices] = {};
