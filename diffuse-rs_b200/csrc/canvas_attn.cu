@@ -368,16 +368,13 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   if (CA_PREP_BULK && vec && hd == 256 && bulk_smem <= 112 * 1024) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
-    static bool attr_done[3][kMaxDevices] = {};
-    const int ti = hd == 64 ? 0 : hd == 128 ? 1 : 2;
-    const void* fn = hd == 64 ? reinterpret_cast<const void*>(prep_bulk_kernel<8>)
-                     : hd == 128 ? reinterpret_cast<const void*>(prep_bulk_kernel<16>)
-                                 : reinterpret_cast<const void*>(prep_bulk_kernel<32>);
-    if (!attr_done[ti][dev]) {
+    static bool attr_done[kMaxDevices] = {};
+    const void* fn = reinterpret_cast<const void*>(prep_bulk_kernel<32>);
+    if (!attr_done[dev]) {
       if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024) !=
           cudaSuccess)
         return CA_ERR_CUDA;
-      attr_done[ti][dev] = true;
+      attr_done[dev] = true;
     }
     // Exactly one wave of resident CTAs (they stride over the tokens).
     int per_sm = 1, n_sm = 148;
@@ -387,9 +384,7 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
       per_sm = 1;
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
     const int blocks = static_cast<int>(std::min<long long>(toks, 1LL * n_sm * per_sm));
-    if (hd == 64) prep_bulk_kernel<8><<<blocks, kPrepThreads, bulk_smem, st>>>(pp);
-    else if (hd == 128) prep_bulk_kernel<16><<<blocks, kPrepThreads, bulk_smem, st>>>(pp);
-    else prep_bulk_kernel<32><<<blocks, kPrepThreads, bulk_smem, st>>>(pp);
+    prep_bulk_kernel<32><<<blocks, kPrepThreads, bulk_smem, st>>>(pp);
   } else if (vec && (hd == 64 || hd == 128 || hd == 256)) {
     // 16-row jobs unless that leaves fewer jobs than 64 warps per SM; then
     // one warp step per job (256 / head_dim rows).

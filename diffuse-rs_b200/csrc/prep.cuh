@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(256) prep_pair_kernel(const PrepParams p) {
   }
 }
 
-// Bulk-copy form (head_dim 64 / 128 / 256, rope_dim % 16 == 0, 16-byte
+// Bulk-copy form (dispatched at head_dim 256; rope_dim % 16 == 0, 16-byte
 // aligned Q/K/V): one producer lane per CTA streams each token's Q, K and V
 // rows (contiguous in the inputs: H, Hkv and Hkv rows of head_dim) into a
 // ring of kPrepStages shared-memory stages with cp.async.bulk, so many
