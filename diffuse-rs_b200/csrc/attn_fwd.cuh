@@ -40,6 +40,7 @@ namespace ca {
 constexpr int kNoWindow = INT_MAX;
 
 constexpr int kMaxPeers = 7;  // other GPUs of one 8-GPU box
+constexpr int kFwdThreads = 352;  // 3 control warps + 8 softmax warps
 
 struct FwdParams {
   void* out;
@@ -87,11 +88,7 @@ struct FwdParams {
 //           columns and half of O (head_dim 256: TMEM holds one O)
 //   kAlt    group g takes key tiles g, g+2, ... with its own S/P buffer and
 //           O, merged at the end (head_dim <= 192)
-//   kOne    one softmax group (four warps) taking every key tile, S double-
-//           buffered, one O; half the TMEM and about half the shared memory
-//           of kAlt, so two CTAs share an SM and one's prologue and epilogue
-//           overlap the other's main loop (head_dim 128, 64-key tiles)
-enum FwdMode { kSplit = 0, kAlt = 1, kOne = 3 };
+enum FwdMode { kSplit = 0, kAlt = 1 };
 
 
 template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_, int STK_ = ST_, int KSUB_ = 1,
@@ -107,11 +104,6 @@ struct FwdCfg {
   static constexpr int MODE = MODE_;
   static constexpr bool ALT = MODE == kAlt;
   static constexpr bool SPLIT = MODE == kSplit;
-  static constexpr bool ONE = MODE == kOne;
-  static constexpr int kGroups = ONE ? 1 : 2;                // softmax groups of four warps
-  static constexpr int kSoftThreads = 128 * kGroups;
-  static constexpr int kThreads = 96 + kSoftThreads;         // + 3 control warps
-  static constexpr int kMinBlocks = ONE ? 2 : 1;             // CTAs per SM
   static constexpr int kPTerms = PRECISE ? 2 : 1;
   // Wide heads (head_dim > 256): OS CTAs share one Q tile, each computing
   // S = Q K^T over the whole head and owning HDO = HDP / OS columns of O
@@ -163,12 +155,11 @@ struct FwdCfg {
   static constexpr int kOffMisc = kOffXch + kXchBytes;
   static constexpr int kMiscBytes = 64;
   static constexpr int kSmemBytes = kOffMisc + kMiscBytes;
-  static constexpr int kTmemCols = ONE ? 256 : 512;
+  static constexpr int kTmemCols = 512;
   static constexpr int kOCol = SB * BN;  // O accumulator(s) after the S buffers
   static constexpr uint32_t kIdescS = umma_idesc_bf16(128, BN, 0, 0);
   static constexpr uint32_t kIdescO = umma_idesc_bf16(128, HDO, 0, 1);
-  static_assert(kOCol + ((SPLIT || ONE) ? 1 : 2) * HDO <= kTmemCols, "TMEM budget");
-  static_assert(!ONE || (OS == 1 && KSUB == 1 && VSUB == 1), "one group: whole-tile units");
+  static_assert(kOCol + (SPLIT ? 1 : 2) * HDO <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 512, "tile shape");
   static_assert(HDO % 64 == 0 && HDO <= 256 && kChunks % KSUB == 0 && BN % (16 * VSUB) == 0,
@@ -528,14 +519,14 @@ __device__ __forceinline__ void store_peers(const FwdParams& p, int64_t off, uin
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_o, const FwdParams p,
                     const __grid_constant__ PeerMaps pm) {
   constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST, STK = C::STK;
-  constexpr bool ALT = C::ALT, SPLIT = C::SPLIT, ONE = C::ONE;
+  constexpr bool ALT = C::ALT, SPLIT = C::SPLIT;
   // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
   // static shared memory, so the dynamic window starts 1024-aligned; if it
   // ever did not, report it instead of computing garbage.
@@ -680,7 +671,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
           const int u = j * C::KSUB + part;
           const int s = u % STK;
           if (!mbar_wait(bar(C::kBarK + s), (u / STK) & 1, dead, p.err)) return false;
-          if (part == 0 && (ALT || ONE) && j >= 2 &&
+          if (part == 0 && ALT && j >= 2 &&
               !mbar_wait(bar(C::kBarO + og(j - 2)), ouse(j - 2) & 1, dead, p.err))
             return false;
           tc_fence_after();
@@ -788,7 +779,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     float m = -INFINITY, l = 0.f;
     int used = 0;  // tiles this thread has processed
 
-    if constexpr (HDP == 128 && !ONE) {
+    if constexpr (HDP == 128) {
       if (p.fuse_q) fuse_q_prep<C>(p, sQ, bar(C::kBarQ), bar(C::kBarQR), t0, q_beg, q_len,
                                    (warp - 3) * 32 + lane, dead);
     }
@@ -1047,8 +1038,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
                   x0 = vis(msk_c, cb * LB + i) ? x0 : -INFINITY;
                   x1 = vis(msk_c, cb * LB + i + 1) ? x1 : -INFINITY;
                 }
-                if constexpr ((ALT || ONE) && V == kPlain && M == kNone && !C::PRECISE &&
-                              CA_POLY_EVERY > 0) {
+                if constexpr (ALT && V == kPlain && M == kNone && !C::PRECISE && CA_POLY_EVERY > 0) {
                   if (q2 % kPolyEvery == kPolyEvery - 1) {
                     const float2 e = ex2_poly3x2(x0, x1);
                     emit(e.x, e.y, q2, hi[q2], lo[q2]);
@@ -1083,15 +1073,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
           tc_fence_after();
         }
       }
-      // Lazy correction of O (rare after the first tiles). kOne: the
-      // previous tile's P V may still accumulate into O; wait for it first.
+      // Lazy correction of O (rare after the first tiles).
       if (used > 0 && __any_sync(0xffffffffu, resc)) {
-        if constexpr (ONE) {
-          mbar_wait(bar(C::kBarO), (j - 1) & 1, dead, p.err);
-          dead = __any_sync(0xffffffffu, dead);
-          if (dead) break;
-          tc_fence_after();
-        }
 #pragma unroll 1
         for (int c = 0; c < OC / 32; ++c) {
           uint32_t o[32];
@@ -1134,9 +1117,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     float s_me = 1.f, s_ot = 0.f, inv = __int_as_float(0x7fc00000);
     const int n_me = ALT ? (grp == 0 ? (n + 1) / 2 : n / 2) : n;
     const int n_ot = ALT ? (grp == 0 ? n / 2 : (n + 1) / 2) : 0;
-    if (have && ONE) {
-      inv = 1.f / l;  // a single group owns every row and column
-    } else if (have) {
+    if (have) {
       // kAlt: [group][l, m][128].
       float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
       float* xo = ALT ? xch + grp * 256 : xch + ((n & 1) * 2 + grp) * 128;
@@ -1164,8 +1145,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     const int head = kvh * p.G + (r % p.G);
     // Columns this warp writes: kAlt half of the columns from both
     // accumulators; kSplit its own half.
-    constexpr int WC = ONE ? C::HDO : C::HDO / 2;
-    const int col0 = ONE ? 0 : grp * WC;
+    constexpr int WC = C::HDO / 2;
+    const int col0 = grp * WC;
     const uint32_t o_me = ALT ? C::kOCol + grp * C::HDO + col0 : o_own;
     const uint32_t o_ot = C::kOCol + (grp ^ 1) * C::HDO + col0;
     const int ocol = ohalf * C::HDO;  // this CTA's first output column
@@ -1260,7 +1241,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     if (p.tma_out) {
       // All softmax warps have staged their rows: one thread stores the tile.
       fence_proxy_async_smem();
-      named_bar_sync(2, C::kSoftThreads);
+      named_bar_sync(2, 256);
       if (warp == 3 && lane == 0) {
         const int inner = p.out_f32 ? 32 : 64;  // elements per 128-byte chunk
         for (int ci = 0; ci * inner < C::HDO && ocol + ci * inner < p.hd; ++ci) {

@@ -136,16 +136,11 @@ struct Launch {
       if (cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::kSmemBytes) != cudaSuccess)
         return CA_ERR_CUDA;
-      // Configurations meant to share an SM ask for the whole carve-out.
-      if (C::kMinBlocks > 1 &&
-          cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                               100) != cudaSuccess)
-        return CA_ERR_CUDA;
       attr_done[dev] = true;
     }
     const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
     dim3 grid(n_qtiles * C::OS, p->n_head_kv, p->batch);
-    attn_fwd_kernel<C><<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, to, pl, pm);
+    attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, to, pl, pm);
     return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
   }
 };
@@ -162,9 +157,6 @@ int clamp_opt(int64_t v) {  // Option<usize> as int32 (None = -1)
 // Fused Q pre-ops for the block path (see FwdParams::fuse_q).
 #ifndef CA_FUSE_Q
 #define CA_FUSE_Q 1
-#endif
-#ifndef CA_ONE
-#define CA_ONE 0
 #endif
 #ifndef CA_PREP_BULK
 #define CA_PREP_BULK 1
@@ -275,12 +267,6 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
     return a->precise ? L.run<FwdCfg<512, 64, 2, true, kSplit, 3, 4, 2, 2>>()
                       : L.run<FwdCfg<512, 64, 2, false, kSplit, 3, 4, 2, 2>>();
   }
-  // One softmax group per CTA and two CTAs per SM (head_dim 128, Q rotated
-  // outside the kernel).
-  const bool one = CA_ONE && hdp == 128 && !fq;
-  if (one)
-    return a->precise ? L.run<FwdCfg<128, 64, 2, true, kOne>>()
-                      : L.run<FwdCfg<128, 64, 2, false, kOne>>();
   if (a->precise) {
     if (hdp == 64) return L.run<FwdCfg<64, 128, 2, true, kAlt>>();
     if (hdp == 128) return L.run<FwdCfg<128, 128, 2, true, kAlt>>();
