@@ -40,7 +40,6 @@ namespace ca {
 constexpr int kNoWindow = INT_MAX;
 
 constexpr int kMaxPeers = 7;  // other GPUs of one 8-GPU box
-constexpr int kFwdThreads = 352;  // 3 control warps + 8 softmax warps
 
 struct FwdParams {
   void* out;
@@ -88,7 +87,11 @@ struct FwdParams {
 //           columns and half of O (head_dim 256: TMEM holds one O)
 //   kAlt    group g takes key tiles g, g+2, ... with its own S/P buffer and
 //           O, merged at the end (head_dim <= 192)
-enum FwdMode { kSplit = 0, kAlt = 1 };
+//   kOne    one softmax group (four warps) taking every key tile, S double-
+//           buffered, one O; half the TMEM and about half the shared memory
+//           of kAlt, so two CTAs share an SM and one's prologue and epilogue
+//           overlap the other's main loop (head_dim 128, 64-key tiles)
+enum FwdMode { kSplit = 0, kAlt = 1, kOne = 3 };
 
 
 template <int HDP_, int BN_, int ST_, bool PRECISE_, int MODE_, int STK_ = ST_, int KSUB_ = 1,
@@ -104,6 +107,11 @@ struct FwdCfg {
   static constexpr int MODE = MODE_;
   static constexpr bool ALT = MODE == kAlt;
   static constexpr bool SPLIT = MODE == kSplit;
+  static constexpr bool ONE = MODE == kOne;
+  static constexpr int kGroups = ONE ? 1 : 2;                // softmax groups of four warps
+  static constexpr int kSoftThreads = 128 * kGroups;
+  static constexpr int kThreads = 96 + kSoftThreads;         // + 3 control warps
+  static constexpr int kMinBlocks = ONE ? 2 : 1;             // CTAs per SM
   static constexpr int kPTerms = PRECISE ? 2 : 1;
   // Wide heads (head_dim > 256): OS CTAs share one Q tile, each computing
   // S = Q K^T over the whole head and owning HDO = HDP / OS columns of O
@@ -155,11 +163,12 @@ struct FwdCfg {
   static constexpr int kOffMisc = kOffXch + kXchBytes;
   static constexpr int kMiscBytes = 64;
   static constexpr int kSmemBytes = kOffMisc + kMiscBytes;
-  static constexpr int kTmemCols = 512;
+  static constexpr int kTmemCols = ONE ? 256 : 512;
   static constexpr int kOCol = SB * BN;  // O accumulator(s) after the S buffers
   static constexpr uint32_t kIdescS = umma_idesc_bf16(128, BN, 0, 0);
   static constexpr uint32_t kIdescO = umma_idesc_bf16(128, HDO, 0, 1);
-  static_assert(kOCol + (SPLIT ? 1 : 2) * HDO <= kTmemCols, "TMEM budget");
+  static_assert(kOCol + (ALT ? 2 : 1) * HDO <= kTmemCols, "TMEM budget");
+  static_assert(!ONE || (OS == 1 && KSUB == 1 && VSUB == 1), "one group: whole-tile units");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(BN % 64 == 0 && BN <= 256 && HDP % 64 == 0 && HDP <= 512, "tile shape");
   static_assert(HDO % 64 == 0 && HDO <= 256 && kChunks % KSUB == 0 && BN % (16 * VSUB) == 0,
@@ -416,87 +425,116 @@ __device__ void build_tile_list(const FwdParams& p, int b, int q_beg, int q_len,
 
 namespace ca {
 
-// Fused Q pre-ops, run by the 256 softmax threads once the raw Q tile has
-// landed: thread tt owns row tt / 2 and the NeoX pairs (i, i + 64) for i in
-// 32 (tt & 1) .. +31, i.e. 16-byte units of both 64-column chunks of the
-// 128-byte-swizzled tile (unit u of row r sits at u ^ (r & 7)). Arithmetic is
-// that of the pre-ops kernel (norm_heads / rms_norm_inplace, src/model/ops.rs:
-// 107-114, 385-389; rotate_rows :432-452): f32 squares summed in f64 (exact
-// for bf16 inputs), scale = 1 / (float)sqrt(ss / 128 + eps), x * scale * w,
+// Fused Q pre-ops, run by the softmax threads once the raw Q tile has
+// landed. With two softmax groups (256 threads) thread tt owns row tt / 2 and
+// the NeoX pairs (i, i + 64) for i in 32 (tt & 1) .. +31; with one group (128
+// threads) thread tt owns the whole row tt. A thread's columns are 16-byte
+// units of both 64-column chunks of the 128-byte-swizzled tile (unit u of row
+// r sits at u ^ (r & 7)). Arithmetic is that of the pre-ops kernel
+// (norm_heads / rms_norm_inplace, src/model/ops.rs:107-114, 385-389;
+// rotate_rows :432-452): f32 squares summed in f64 (exact for bf16 inputs;
+// the two 32-column halves' sums are added last in both forms, so both give
+// the same bits), scale = 1 / (float)sqrt(ss / 128 + eps), x * scale * w,
 // then (a, b) -> (a cos - b sin, a sin + b cos), rounded to bf16 in place.
-// The writes are fenced for the tensor core's (async) proxy, the 256 threads
-// meet at a named barrier and one arrival releases the first Q K^T.
+// The writes are fenced for the tensor core's (async) proxy, the softmax
+// threads meet at a named barrier and one arrival releases the first Q K^T.
 template <class C>
 __device__ __forceinline__ void fuse_q_prep(const FwdParams& p, uint32_t sQ, uint32_t bar_q,
                                             uint32_t bar_qr, int t0, int q_beg, int q_len,
                                             int tt, bool& dead) {
+  constexpr int TPR = C::ONE ? 1 : 2;  // threads per Q row
+  constexpr int NH = 2 / TPR;          // 32-column halves per thread
   mbar_wait(bar_q, 0, dead, p.err);
-  const int r = tt >> 1, h = tt & 1;
+  const int r = tt / TPR, h0 = tt % TPR;
   const int t_local = t0 + r / p.G;
   const bool valid = !dead && r < p.R && t_local < q_len;
-  // Four 16-byte units per chunk: units 4h .. 4h + 3 (columns 32h .. 32h + 31).
-  uint32_t lo[16], hi[16];
+  // Four 16-byte units per chunk and half: units 4h .. 4h + 3 (columns
+  // 32h .. 32h + 31).
+  uint32_t lo[NH][16], hi[NH][16];
   const uint32_t row_lo = sQ + r * 128, row_hi = sQ + C::kQChunk + r * 128;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) lo[i] = hi[i] = 0u;
+  for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) lo[hh][i] = hi[hh][i] = 0u;
   if (valid) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t off = static_cast<uint32_t>(((4 * h + u) ^ (r & 7)) << 4);
-      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(lo[4 * u]), "=r"(lo[4 * u + 1]), "=r"(lo[4 * u + 2]), "=r"(lo[4 * u + 3])
-                   : "r"(row_lo + off));
-      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(hi[4 * u]), "=r"(hi[4 * u + 1]), "=r"(hi[4 * u + 2]), "=r"(hi[4 * u + 3])
-                   : "r"(row_hi + off));
+    for (int hh = 0; hh < NH; ++hh) {
+      const int h = h0 + hh;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t off = static_cast<uint32_t>(((4 * h + u) ^ (r & 7)) << 4);
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(lo[hh][4 * u]), "=r"(lo[hh][4 * u + 1]), "=r"(lo[hh][4 * u + 2]),
+                       "=r"(lo[hh][4 * u + 3])
+                     : "r"(row_lo + off));
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(hi[hh][4 * u]), "=r"(hi[hh][4 * u + 1]), "=r"(hi[hh][4 * u + 2]),
+                       "=r"(hi[hh][4 * u + 3])
+                     : "r"(row_hi + off));
+      }
     }
   }
-  double ss = 0.0;
+  double sh[NH];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float a0 = __uint_as_float(lo[i] << 16), a1 = __uint_as_float(lo[i] & 0xffff0000u);
-    const float b0 = __uint_as_float(hi[i] << 16), b1 = __uint_as_float(hi[i] & 0xffff0000u);
-    ss += static_cast<double>(__fmul_rn(a0, a0));
-    ss += static_cast<double>(__fmul_rn(a1, a1));
-    ss += static_cast<double>(__fmul_rn(b0, b0));
-    ss += static_cast<double>(__fmul_rn(b1, b1));
+  for (int hh = 0; hh < NH; ++hh) {
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float a0 = __uint_as_float(lo[hh][i] << 16);
+      const float a1 = __uint_as_float(lo[hh][i] & 0xffff0000u);
+      const float b0 = __uint_as_float(hi[hh][i] << 16);
+      const float b1 = __uint_as_float(hi[hh][i] & 0xffff0000u);
+      ss += static_cast<double>(__fmul_rn(a0, a0));
+      ss += static_cast<double>(__fmul_rn(a1, a1));
+      ss += static_cast<double>(__fmul_rn(b0, b0));
+      ss += static_cast<double>(__fmul_rn(b1, b1));
+    }
+    sh[hh] = ss;
   }
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);  // the row's other half (adjacent lane)
+  double ss;
+  if constexpr (TPR == 2) ss = sh[0] + __shfl_xor_sync(0xffffffffu, sh[0], 1);  // other half
+  else ss = sh[0] + sh[NH - 1];
   if (valid) {
     const int pos = p.q_pos ? p.q_pos[q_beg + t_local] : t_local;
     const bool norm = p.fq_w != nullptr;
     const float sc =
         __fdiv_rn(1.f, static_cast<float>(sqrt(ss / 128.0 + static_cast<double>(p.fq_eps))));
-    const float* cs_row = p.fq_rope + 2 * (static_cast<long long>(pos) * 64 + 32 * h);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float a[2] = {__uint_as_float(lo[i] << 16), __uint_as_float(lo[i] & 0xffff0000u)};
-      float b[2] = {__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xffff0000u)};
-      const float4 t = __ldg(reinterpret_cast<const float4*>(cs_row) + i);  // (sin, cos) x 2
-      const float sn[2] = {t.x, t.z}, cs[2] = {t.y, t.w};
-      float ya[2], yb[2];
+    for (int hh = 0; hh < NH; ++hh) {
+      const int h = h0 + hh;
+      const float* cs_row = p.fq_rope + 2 * (static_cast<long long>(pos) * 64 + 32 * h);
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int col = 32 * h + 2 * i + e;
-        if (norm) {
-          a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(p.fq_w + col));
-          b[e] = __fmul_rn(__fmul_rn(b[e], sc), __ldg(p.fq_w + 64 + col));
+      for (int i = 0; i < 16; ++i) {
+        float a[2] = {__uint_as_float(lo[hh][i] << 16), __uint_as_float(lo[hh][i] & 0xffff0000u)};
+        float b[2] = {__uint_as_float(hi[hh][i] << 16), __uint_as_float(hi[hh][i] & 0xffff0000u)};
+        const float4 t = __ldg(reinterpret_cast<const float4*>(cs_row) + i);  // (sin, cos) x 2
+        const float sn[2] = {t.x, t.z}, cs[2] = {t.y, t.w};
+        float ya[2], yb[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int col = 32 * h + 2 * i + e;
+          if (norm) {
+            a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(p.fq_w + col));
+            b[e] = __fmul_rn(__fmul_rn(b[e], sc), __ldg(p.fq_w + 64 + col));
+          }
+          ya[e] = __fsub_rn(__fmul_rn(a[e], cs[e]), __fmul_rn(b[e], sn[e]));
+          yb[e] = __fadd_rn(__fmul_rn(a[e], sn[e]), __fmul_rn(b[e], cs[e]));
         }
-        ya[e] = __fsub_rn(__fmul_rn(a[e], cs[e]), __fmul_rn(b[e], sn[e]));
-        yb[e] = __fadd_rn(__fmul_rn(a[e], sn[e]), __fmul_rn(b[e], cs[e]));
+        lo[hh][i] = pack_bf16(ya[0], ya[1]);
+        hi[hh][i] = pack_bf16(yb[0], yb[1]);
       }
-      lo[i] = pack_bf16(ya[0], ya[1]);
-      hi[i] = pack_bf16(yb[0], yb[1]);
-    }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t off = static_cast<uint32_t>(((4 * h + u) ^ (r & 7)) << 4);
-      st_shared_v4(row_lo + off, lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
-      st_shared_v4(row_hi + off, hi[4 * u], hi[4 * u + 1], hi[4 * u + 2], hi[4 * u + 3]);
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t off = static_cast<uint32_t>(((4 * h + u) ^ (r & 7)) << 4);
+        st_shared_v4(row_lo + off, lo[hh][4 * u], lo[hh][4 * u + 1], lo[hh][4 * u + 2],
+                     lo[hh][4 * u + 3]);
+        st_shared_v4(row_hi + off, hi[hh][4 * u], hi[hh][4 * u + 1], hi[hh][4 * u + 2],
+                     hi[hh][4 * u + 3]);
+      }
     }
   }
   fence_proxy_async_smem();
-  named_bar_sync(3, 256);
+  named_bar_sync(3, C::kSoftThreads);
   if (tt == 0) mbar_arrive(bar_qr);
 }
 
@@ -519,14 +557,14 @@ __device__ __forceinline__ void store_peers(const FwdParams& p, int64_t off, uin
 }
 
 template <class C>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_o, const FwdParams p,
                     const __grid_constant__ PeerMaps pm) {
   constexpr int BN = C::BN, HDP = C::HDP, ST = C::ST, STK = C::STK;
-  constexpr bool ALT = C::ALT, SPLIT = C::SPLIT;
+  constexpr bool ALT = C::ALT, SPLIT = C::SPLIT, ONE = C::ONE;
   // 128-byte swizzled tiles need 1024-byte aligned bases. The kernel has no
   // static shared memory, so the dynamic window starts 1024-aligned; if it
   // ever did not, report it instead of computing garbage.
@@ -658,7 +696,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       auto ouse = [&](int i) -> int { return ALT ? (i >> 1) : i; };
       // S[j] = Q K_j^T into S buffer j % SB. That buffer last held P[j - SB],
       // so P V[j - SB] must have completed (it reads P from there). kAlt
-      // waits for it here (no later P V on that barrier is issued yet);
+      // and kOne wait for it here (no later P V on that barrier is issued
+      // yet);
       // kSplit issues S[j] after P V[j - 2], whose issue already waited for
       // P V[j - 3].
       // K arrives in KSUB units per tile (one unit for head_dim <= 256), each
@@ -671,8 +710,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int u = j * C::KSUB + part;
           const int s = u % STK;
           if (!mbar_wait(bar(C::kBarK + s), (u / STK) & 1, dead, p.err)) return false;
-          if (part == 0 && ALT && j >= 2 &&
-              !mbar_wait(bar(C::kBarO + og(j - 2)), ouse(j - 2) & 1, dead, p.err))
+          if (part == 0 && !SPLIT && j >= C::SB &&
+              !mbar_wait(bar(C::kBarO + og(j - C::SB)), ouse(j - C::SB) & 1, dead, p.err))
             return false;
           tc_fence_after();
           const uint32_t kbase = sK + s * C::kKUnitBytes;
@@ -1038,7 +1077,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                   x0 = vis(msk_c, cb * LB + i) ? x0 : -INFINITY;
                   x1 = vis(msk_c, cb * LB + i + 1) ? x1 : -INFINITY;
                 }
-                if constexpr (ALT && V == kPlain && M == kNone && !C::PRECISE && CA_POLY_EVERY > 0) {
+                if constexpr ((ALT || ONE) && V == kPlain && M == kNone && !C::PRECISE &&
+                              CA_POLY_EVERY > 0) {
                   if (q2 % kPolyEvery == kPolyEvery - 1) {
                     const float2 e = ex2_poly3x2(x0, x1);
                     emit(e.x, e.y, q2, hi[q2], lo[q2]);
@@ -1066,6 +1106,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // wait also keeps the O barrier from running two phases ahead of any
       // waiter (P V[j] cannot start before this warp's P arrival below).
       if constexpr (SPLIT) {
+        if (used > 0) {
+          mbar_wait(bar(C::kBarO), (j - 1) & 1, dead, p.err);
+          dead = __any_sync(0xffffffffu, dead);
+          if (dead) break;
+          tc_fence_after();
+        }
+      }
+      // kOne: wait for the previous tile's P V. It may still accumulate into
+      // O (which a correction rescales), and its completion shows that the
+      // MMA issuer has taken P[j - 1]: S[j] was issued before P V[j - 1], so
+      // without this wait the group could arrive for P[j] while the issuer
+      // still waits (on V[j - 1]) for P[j - 1], and the P barrier would run
+      // two phases ahead of that parity wait.
+      if constexpr (ONE) {
         if (used > 0) {
           mbar_wait(bar(C::kBarO), (j - 1) & 1, dead, p.err);
           dead = __any_sync(0xffffffffu, dead);
@@ -1117,7 +1171,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     float s_me = 1.f, s_ot = 0.f, inv = __int_as_float(0x7fc00000);
     const int n_me = ALT ? (grp == 0 ? (n + 1) / 2 : n / 2) : n;
     const int n_ot = ALT ? (grp == 0 ? n / 2 : (n + 1) / 2) : 0;
-    if (have) {
+    if (have && ONE) {
+      inv = 1.f / l;  // a single group owns every row and column
+    } else if (have) {
       // kAlt: [group][l, m][128].
       float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
       float* xo = ALT ? xch + grp * 256 : xch + ((n & 1) * 2 + grp) * 128;
@@ -1145,8 +1201,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int head = kvh * p.G + (r % p.G);
     // Columns this warp writes: kAlt half of the columns from both
     // accumulators; kSplit its own half.
-    constexpr int WC = C::HDO / 2;
-    const int col0 = grp * WC;
+    constexpr int WC = ONE ? C::HDO : C::HDO / 2;
+    const int col0 = ONE ? 0 : grp * WC;
     const uint32_t o_me = ALT ? C::kOCol + grp * C::HDO + col0 : o_own;
     const uint32_t o_ot = C::kOCol + (grp ^ 1) * C::HDO + col0;
     const int ocol = ohalf * C::HDO;  // this CTA's first output column
@@ -1241,7 +1297,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (p.tma_out) {
       // All softmax warps have staged their rows: one thread stores the tile.
       fence_proxy_async_smem();
-      named_bar_sync(2, 256);
+      named_bar_sync(2, C::kSoftThreads);
       if (warp == 3 && lane == 0) {
         const int inner = p.out_f32 ? 32 : 64;  // elements per 128-byte chunk
         for (int ci = 0; ci * inner < C::HDO && ocol + ci * inner < p.hd; ++ci) {

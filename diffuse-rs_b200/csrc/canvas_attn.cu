@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdint>
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -136,11 +137,16 @@ struct Launch {
       if (cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::kSmemBytes) != cudaSuccess)
         return CA_ERR_CUDA;
+      // Configurations meant to share an SM ask for the whole carve-out.
+      if (C::kMinBlocks > 1 &&
+          cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               100) != cudaSuccess)
+        return CA_ERR_CUDA;
       attr_done[dev] = true;
     }
     const int n_qtiles = (max_sq + p->QT - 1) / p->QT;
     dim3 grid(n_qtiles * C::OS, p->n_head_kv, p->batch);
-    attn_fwd_kernel<C><<<grid, kFwdThreads, C::kSmemBytes, st>>>(tq, tk, tv, to, pl, pm);
+    attn_fwd_kernel<C><<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, to, pl, pm);
     return cudaGetLastError() == cudaSuccess ? CA_OK : CA_ERR_CUDA;
   }
 };
@@ -267,6 +273,19 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
     return a->precise ? L.run<FwdCfg<512, 64, 2, true, kSplit, 3, 4, 2, 2>>()
                       : L.run<FwdCfg<512, 64, 2, false, kSplit, 3, 4, 2, 2>>();
   }
+  // One softmax group per CTA and two CTAs per SM (head_dim 128) for grids
+  // of at least two CTAs per SM whose CTAs see few keys: one CTA's prologue
+  // and epilogue then overlap the other's main loop. Measured on B200: c2
+  // (16 key tiles of 64 per CTA) 556 -> 616 TFLOP/s; with 32+ tiles of 128
+  // (c3) the two-group kernel is 2% faster, and with one CTA per SM (c4)
+  // the half-size rings keep too few bytes in flight (5.0 -> 3.5 TB/s).
+  const int64_t ctas = static_cast<int64_t>((max_sq + p.QT - 1) / p.QT) * Hkv * a->batch;
+  const int64_t keys_seen =
+      p.window != kNoWindow ? std::min<int64_t>(max_sk, 2LL * p.window + p.QT) : max_sk;
+  const bool one = hdp == 128 && ctas >= 2 * 148 && keys_seen <= 2048;
+  if (one)
+    return a->precise ? L.run<FwdCfg<128, 64, 2, true, kOne>>()
+                      : L.run<FwdCfg<128, 64, 2, false, kOne>>();
   if (a->precise) {
     if (hdp == 64) return L.run<FwdCfg<64, 128, 2, true, kAlt>>();
     if (hdp == 128) return L.run<FwdCfg<128, 128, 2, true, kAlt>>();
