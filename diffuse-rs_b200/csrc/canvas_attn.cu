@@ -164,6 +164,9 @@ int clamp_opt(int64_t v) {  // Option<usize> as int32 (None = -1)
 #ifndef CA_FUSE_Q
 #define CA_FUSE_Q 1
 #endif
+#ifndef CA_PREP_RING
+#define CA_PREP_RING 1
+#endif
 #ifndef CA_PREP_BULK
 #define CA_PREP_BULK 1
 #endif
@@ -384,7 +387,45 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   // both forms are bound by the per-row arithmetic (f64 sum of squares,
   // shuffles), not by bytes in flight, and the token kernel measured 1.6%
   // faster (c3 block 1.345 vs 1.366 ms).
-  if (CA_PREP_BULK && vec && hd == 256 && bulk_smem <= 112 * 1024) {
+  // Ring form for full rotation on passes of at least 256K rows (c3: 1.6M
+  // rows 0.245 -> 0.155 ms; c5: 1.0M rows per layer, 11.77 -> 11.32 ms per
+  // step): as many tokens per stage as fit in 48 KB of rows (at most 16).
+  // Short passes (c2's 32K and c4's 8K rows of K and V) measured 3-5 us
+  // faster on the token kernel, whose many small jobs start at once.
+  int ring_t = 0;
+  if (vec && a->rope_dim == hd && (hd == 64 || hd == 128 || hd == 256) &&
+      jobs >= 256LL * 1024) {
+    const long long tok_bytes = static_cast<long long>(Hp + 2 * Hkv) * hd * 2;
+    ring_t = static_cast<int>(std::min<long long>(16, 48 * 1024 / tok_bytes));
+    while (ring_t > 0 && ring_smem_bytes(ring_t, Hp + 2 * Hkv, hd) > 227 * 1024) --ring_t;
+  }
+  if (CA_PREP_RING && ring_t > 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
+    const void* fn = hd == 64    ? reinterpret_cast<const void*>(prep_ring_kernel<64>)
+                     : hd == 128 ? reinterpret_cast<const void*>(prep_ring_kernel<128>)
+                                 : reinterpret_cast<const void*>(prep_ring_kernel<256>);
+    const int fi = hd == 64 ? 0 : hd == 128 ? 1 : 2;
+    static bool ring_attr[kMaxDevices][3] = {};
+    const size_t smem = ring_smem_bytes(ring_t, Hp + 2 * Hkv, hd);
+    if (!ring_attr[dev][fi]) {
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+          cudaSuccess)
+        return CA_ERR_CUDA;
+      ring_attr[dev][fi] = true;
+    }
+    int per_sm = 1, n_sm = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kRingThreads, smem) !=
+            cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const long long n_stage = (toks + ring_t - 1) / ring_t;
+    const int blocks = static_cast<int>(std::min<long long>(n_stage, 1LL * n_sm * per_sm));
+    if (hd == 64) prep_ring_kernel<64><<<blocks, kRingThreads, smem, st>>>(pp, ring_t);
+    else if (hd == 128) prep_ring_kernel<128><<<blocks, kRingThreads, smem, st>>>(pp, ring_t);
+    else prep_ring_kernel<256><<<blocks, kRingThreads, smem, st>>>(pp, ring_t);
+  } else if (CA_PREP_BULK && vec && hd == 256 && bulk_smem <= 112 * 1024) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CA_ERR_CUDA;
     static bool attr_done[kMaxDevices] = {};

@@ -580,6 +580,239 @@ __global__ void __launch_bounds__(kPrepThreads) prep_bulk_kernel(const PrepParam
 }
 
 
+// Ring form for full rotation (rope_dim == head_dim, head_dim 64 / 128 / 256,
+// 16-byte aligned rows). One producer lane per CTA streams T tokens per
+// stage into a ring of kRingStages shared-memory stages: their Q rows, K rows
+// and V rows (three cp.async.bulk copies: tokens are contiguous in each
+// input), their positions (read by the producer and written beside the rows)
+// and each token's row of the (sin, cos) table (one bulk copy per token), so
+// no consumer waits on a dependent global load. kRingConsumers warps take the
+// staged row groups round-robin across stages. A row spans LPR = head_dim / 32
+// lanes and each lane owns four 16-byte chunks of it, chunk c * LPR + sl (c =
+// 0..3, sl = lane within the row): chunks c and c + 2 are NeoX partners
+// (element i and i + head_dim / 2), so every rotation pair is inside one lane
+// and the only cross-lane step is the row's sum of squares (log2 LPR
+// shuffles). Rows a multiple of 128 bytes apart would read the same banks, so
+// each row of a bank phase walks its chunks in an order XOR-ed with its row
+// index and the loaded registers are put back in order with selects.
+// Arithmetic is the reference's, as in the other forms: f32 squares summed in
+// f64 (exact for bf16 inputs), scale = 1 / (float) sqrt(ss / head_dim + eps),
+// x * scale * w, then (a cos - b sin, a sin + b cos) with separately rounded
+// products.
+constexpr int kRingStages = 4;
+constexpr int kRingConsumers = 16;  // warps
+constexpr int kRingThreads = 32 * (kRingConsumers + 1);
+
+// Shared memory of one stage: rows, then T positions (16-byte padded), then T
+// table rows of head_dim floats.
+__host__ __device__ inline uint32_t ring_stage_bytes(int T, int rows_tok, int hd) {
+  return static_cast<uint32_t>(T) * rows_tok * hd * 2 + ((T * 4 + 15) / 16) * 16 +
+         static_cast<uint32_t>(T) * hd * 4;
+}
+__host__ __device__ inline uint32_t ring_smem_bytes(int T, int rows_tok, int hd) {
+  return kRingStages * ring_stage_bytes(T, rows_tok, hd) + 2 * hd * 4 + 16 * kRingStages;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kRingThreads) prep_ring_kernel(const PrepParams p, int T) {
+  constexpr int LPR = HD / 32;   // lanes per row
+  constexpr int RPW = 32 / LPR;  // rows per warp step (one row group)
+  constexpr int SWZ = 8 / LPR;   // rows sharing one 8-lane bank phase
+  constexpr int Q4 = HD / 4;     // elements between a lane's consecutive chunks
+  extern __shared__ __align__(128) uint8_t prep_ring[];
+  const int rows_tok = p.H + 2 * p.Hkv;
+  const int stage_rows = T * rows_tok;
+  const uint32_t row_bytes = static_cast<uint32_t>(stage_rows) * HD * 2;
+  const uint32_t pos_off = row_bytes, tab_off = row_bytes + ((T * 4 + 15) / 16) * 16;
+  const uint32_t stage_bytes = ring_stage_bytes(T, rows_tok, HD);
+  float* w_s = reinterpret_cast<float*>(prep_ring + kRingStages * stage_bytes);  // [2][HD]
+  const uint32_t ring = smem_u32(prep_ring);
+  const uint32_t bars = ring + kRingStages * stage_bytes + 2 * HD * 4;  // full[S], empty[S]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long n_tok = prep_tokens(p);
+  const long long n_stage = (n_tok + T - 1) / T;
+  const int groups = (stage_rows + RPW - 1) / RPW;  // row groups per stage
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRingStages; ++s) {
+      mbar_init(bars + 8 * s, 1);
+      mbar_init(bars + 8 * (kRingStages + s), kRingConsumers);
+    }
+    fence_barrier_init();
+  }
+  for (int e = threadIdx.x; e < HD; e += blockDim.x) {
+    w_s[e] = p.q_norm_w ? p.q_norm_w[e] : 1.f;
+    w_s[HD + e] = p.k_norm_w ? p.k_norm_w[e] : 1.f;
+  }
+  __syncthreads();
+  bool dead = false;
+  if (warp == kRingConsumers) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int it = 0;
+      for (long long g = blockIdx.x; g < n_stage; g += gridDim.x, ++it) {
+        const int s = it % kRingStages;
+        if (it >= kRingStages &&
+            !mbar_wait(bars + 8 * (kRingStages + s), ((it / kRingStages) - 1) & 1, dead, p.err))
+          break;
+        const long long tok0 = g * T;
+        const int nt = static_cast<int>(min(static_cast<long long>(T), n_tok - tok0));
+        const uint32_t dst = ring + s * stage_bytes;
+        int* pos_s = reinterpret_cast<int*>(prep_ring + s * stage_bytes + pos_off);
+        mbar_arrive_expect_tx(bars + 8 * s, static_cast<uint32_t>(nt) * (rows_tok * HD * 2 + HD * 4));
+        if (p.H > 0)
+          bulk_load(dst, p.q + tok0 * p.H * HD, nt * p.H * HD * 2, bars + 8 * s);
+        bulk_load(dst + T * p.H * HD * 2, p.k + tok0 * p.Hkv * HD, nt * p.Hkv * HD * 2,
+                  bars + 8 * s);
+        bulk_load(dst + T * (p.H + p.Hkv) * HD * 2, p.v + tok0 * p.Hkv * HD,
+                  nt * p.Hkv * HD * 2, bars + 8 * s);
+        for (int t = 0; t < nt; ++t) {
+          const int pos = __ldg(p.pos + tok0 + t);
+          pos_s[t] = pos;  // ordered before the consumers' reads by the stage barrier
+          bulk_load(dst + tab_off + t * HD * 4, p.rope + static_cast<long long>(pos) * HD,
+                    HD * 4, bars + 8 * s);
+        }
+      }
+      // Leave no bulk copy in flight: wait (bounded) for the last stages.
+      bool d2 = false;
+      for (int j = it > kRingStages ? it - kRingStages : 0; j < it; ++j)
+        mbar_wait(bars + 8 * (j % kRingStages), (j / kRingStages) & 1, d2, p.err);
+    }
+    return;
+  }
+  // ------------------------------------------------------------ consumers
+  const int sub = lane / LPR, sl = lane % LPR;
+  const int sw = sub % SWZ;  // chunk-order XOR of this lane's row
+  int it = 0;
+  long long gbase = 0;  // this CTA's row groups before the current stage
+  for (long long g = blockIdx.x; g < n_stage; g += gridDim.x, ++it, gbase += groups) {
+    const int s = it % kRingStages;
+    if (!mbar_wait(bars + 8 * s, (it / kRingStages) & 1, dead, p.err)) break;
+    const long long tok0 = g * T;
+    const int nt = static_cast<int>(min(static_cast<long long>(T), n_tok - tok0));
+    const uint8_t* stage = prep_ring + s * stage_bytes;
+    const int* pos_s = reinterpret_cast<const int*>(stage + pos_off);
+    // Row groups k of this stage with (gbase + k) % consumers == warp.
+    const int k0 = static_cast<int>((warp - gbase % kRingConsumers + kRingConsumers) %
+                                    kRingConsumers);
+    for (int k = k0; k < groups; k += kRingConsumers) {
+      const int i = k * RPW + sub;  // row of the stage
+      int kind, t, h;               // 0 Q, 1 K, 2 V; token in the stage; head
+      if (i < T * p.H) {
+        kind = 0; t = i / p.H; h = i - t * p.H;
+      } else if (i < T * (p.H + p.Hkv)) {
+        const int j = i - T * p.H;
+        kind = 1; t = j / p.Hkv; h = j - t * p.Hkv;
+      } else {
+        const int j = i - T * (p.H + p.Hkv);
+        kind = 2; t = j / p.Hkv; h = j - t * p.Hkv;
+      }
+      const bool valid = i < stage_rows && t < nt;
+      // Chunks in bank-spread order, then back in logical order.
+      const uint8_t* src = stage + static_cast<size_t>(valid ? i : 0) * HD * 2;
+      uint4 raw[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        raw[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw) * LPR + sl) * 16);
+      if (sw & 1) {
+        const uint4 t0 = raw[0], t2 = raw[2];
+        raw[0] = raw[1]; raw[1] = t0; raw[2] = raw[3]; raw[3] = t2;
+      }
+      if (SWZ > 2 && (sw & 2)) {
+        const uint4 t0 = raw[0], t1 = raw[1];
+        raw[0] = raw[2]; raw[1] = raw[3]; raw[2] = t0; raw[3] = t1;
+      }
+      float x[32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t wv[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          x[c * 8 + 2 * e] = __uint_as_float(wv[e] << 16);
+          x[c * 8 + 2 * e + 1] = __uint_as_float(wv[e] & 0xffff0000u);
+        }
+      }
+      const bool weighted = kind == 0 ? p.q_norm_w != nullptr
+                                      : kind == 1 ? p.k_norm_w != nullptr : false;
+      const bool norm = valid && (kind == 2 ? p.v_norm != 0 : weighted);
+      // Four independent chains; each term is an exact f32 square, so the
+      // f64 sums are exact for the rows bf16 inputs form and the order is free.
+      double ss = 0.0;
+      if (norm) {
+        double s4[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const double d = static_cast<double>(x[e]);
+          s4[e & 3] = fma(d, d, s4[e & 3]);  // == s + (double)(x * x)
+        }
+        ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      }
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (!valid) continue;
+      const long long tok = tok0 + t;
+      const int pos = pos_s[t];
+      if (norm) {
+        const float sc =
+            __fdiv_rn(1.f, static_cast<float>(sqrt(ss / HD + static_cast<double>(p.eps))));
+        if (weighted) {
+          const float* w = w_s + (kind == 0 ? 0 : HD);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float4 w0 = *reinterpret_cast<const float4*>(w + c * Q4 + sl * 8);
+            const float4 w1 = *reinterpret_cast<const float4*>(w + c * Q4 + sl * 8 + 4);
+            const float wf[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[c * 8 + e] = __fmul_rn(__fmul_rn(x[c * 8 + e], sc), wf[e]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[e] = __fmul_rn(x[e], sc);
+        }
+      }
+      __nv_bfloat16* dst;
+      if (kind == 0) {
+        dst = p.q_out + (tok * p.H + h) * HD;
+      } else {
+        const long long crow = cache_row(p, tok, pos);
+        dst = (kind == 1 ? p.cache_k : p.cache_v) + (crow * p.Hkv + h) * HD;
+      }
+      if (kind != 2) {  // V is not rotated (forward.rs:310 rotates Q and K only)
+        // Chunks c and c + 2 (c = 0, 1) pair up; chunk c's elements use table
+        // entries c * Q4 + sl * 8 .. + 7 of the token's staged row.
+        const float* tab = reinterpret_cast<const float*>(stage + tab_off) + t * HD;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const float4* t4 = reinterpret_cast<const float4*>(tab + 2 * (c * Q4 + sl * 8));
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = t4[q];  // (sin, cos) of elements 2q, 2q + 1
+            const float sn[2] = {v.x, v.z}, cs[2] = {v.y, v.w};
+#pragma unroll
+            for (int e2 = 0; e2 < 2; ++e2) {
+              const int ia = c * 8 + 2 * q + e2, ib = ia + 16;
+              const float a = x[ia], b = x[ib];
+              x[ia] = __fsub_rn(__fmul_rn(a, cs[e2]), __fmul_rn(b, sn[e2]));
+              x[ib] = __fadd_rn(__fmul_rn(a, sn[e2]), __fmul_rn(b, cs[e2]));
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 o;
+        o.x = pack2_bf16(x[c * 8 + 0], x[c * 8 + 1]);
+        o.y = pack2_bf16(x[c * 8 + 2], x[c * 8 + 3]);
+        o.z = pack2_bf16(x[c * 8 + 4], x[c * 8 + 5]);
+        o.w = pack2_bf16(x[c * 8 + 6], x[c * 8 + 7]);
+        *reinterpret_cast<uint4*>(dst + (c * LPR + sl) * 8) = o;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars + 8 * (kRingStages + s));
+  }
+}
+
+
 // fp32 -> bf16 (round to nearest even), used by the host-buffer entry point.
 __global__ void f32_to_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out,
                                    long long n) {
