@@ -117,3 +117,119 @@ class PeerRows:
         for _, p in self.peers:
             self._ca.ipc_close(p)
         self.peers = []
+
+
+# ---------------------------------------------------------------- failures
+# Host-side failure detection for multi-rank layers. The reference has no
+# multi-process path (its failure handling is request-level); these helpers
+# make a bad or missing rank surface as an error on every rank before any
+# kernel or collective of the next step is launched, instead of a hang.
+
+
+class ShardMismatch(ValueError):
+    """The ranks disagree on a layer's shape or sharding arguments."""
+
+
+class RankFailed(RuntimeError):
+    """Another rank reported a failure (between steps)."""
+
+    def __init__(self, rank: int, what: str):
+        super().__init__(f"rank {rank} failed: {what}")
+        self.rank = rank
+        self.what = what
+
+
+def agree_on_layer(fields: dict, group=None) -> None:
+    """Checks that every rank passes the same layer arguments.
+
+    fields: plain values (ints, floats, strings) describing the call, e.g.
+    tokens, n_head, n_head_kv, head_dim, world. Exchanged with one
+    all_gather_object; on any difference every rank raises ShardMismatch
+    naming the first differing field and the ranks' values, so no rank goes
+    on to launch a layer whose peers would wait for it forever.
+    """
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    mine = tuple(sorted(fields.items()))
+    every = [None] * world
+    dist.all_gather_object(every, mine, group=group)
+    for r, other in enumerate(every):
+        if other != mine:
+            a, b = dict(mine), dict(other)
+            diff = sorted(k for k in set(a) | set(b) if a.get(k) != b.get(k))
+            k = diff[0] if diff else "?"
+            raise ShardMismatch(f"layer arguments differ: {k} = {a.get(k)!r} here, "
+                                f"{b.get(k)!r} on rank {r}")
+
+
+class FailureBoard:
+    """Failure notices between steps, on the process group's key-value store.
+
+    A rank that fails inside `step()` writes `<prefix>/<rank>` before the
+    exception leaves it; every rank calls `check()` before launching the next
+    step and raises RankFailed for the first failed rank it finds. A rank
+    therefore leaves only between steps, with none of its work in flight, and
+    the others learn of it on the host. `wait_for(rank, seconds)` polls until
+    a given rank has reported (tests and drivers that expect a failure).
+    """
+
+    def __init__(self, prefix: str = "ca_fail", store=None, group=None):
+        import torch.distributed as dist
+        from torch.distributed import distributed_c10d as c10d
+
+        self.store = store if store is not None else c10d._get_default_store()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.prefix = prefix
+
+    def _key(self, r: int) -> str:
+        return f"{self.prefix}/{r}"
+
+    def report(self, exc: BaseException) -> None:
+        self.store.set(self._key(self.rank), f"{type(exc).__name__}: {exc}")
+
+    def check(self) -> None:
+        for r in range(self.world):
+            if r != self.rank and self.store.check([self._key(r)]):
+                raise RankFailed(r, self.store.get(self._key(r)).decode())
+
+    def wait_for(self, rank: int, seconds: float) -> None:
+        import time
+
+        deadline = time.monotonic() + seconds
+        while time.monotonic() < deadline:
+            self.check()
+            time.sleep(0.01)
+        raise TimeoutError(f"rank {rank} reported nothing within {seconds} s")
+
+    class _Step:
+        def __init__(self, board):
+            self.board = board
+
+        def __enter__(self):
+            self.board.check()
+            return self
+
+        def __exit__(self, et, ev, tb):
+            if ev is not None and not isinstance(ev, RankFailed):
+                self.board.report(ev)
+            return False
+
+    def step(self):
+        """Context manager for one step: checks the board on entry and
+        reports this rank's exception (and re-raises it) on the way out."""
+        return FailureBoard._Step(self)
+
+
+def init_group(backend: str, rank: int, world: int, timeout_s: float = 60.0) -> None:
+    """init_process_group with a bounded rendezvous and collective timeout:
+    a rank that never joins makes the others' init raise after `timeout_s`
+    instead of waiting forever (and, with NCCL, a collective that does not
+    complete within it is aborted by the process group's watchdog)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    dist.init_process_group(backend, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))

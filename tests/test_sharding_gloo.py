@@ -72,3 +72,78 @@ def test_head_sharded_layer_gathers_to_unsharded_result():
     assert len(result) == world
     for r in range(world):
         assert result[r] == 0.0, result[r]  # same rows, same order: bit-exact
+
+
+# ------------------------------------------------ host-side failure detection
+def _failure_worker(rank, world, port, case, result):
+    import sys
+    import time
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "diffuse-rs_b200")]
+    from canvas_attn.sharding import (FailureBoard, RankFailed, ShardMismatch,
+                                      agree_on_layer, init_group)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    if case == "never_joins":
+        if rank == 1:
+            result[rank] = "stayed away"
+            return
+        t0 = time.monotonic()
+        try:
+            init_group("gloo", rank, world, timeout_s=3.0)
+            result[rank] = "joined"
+        except Exception as e:  # rendezvous timeout
+            result[rank] = f"error after {time.monotonic() - t0:.1f}s: {type(e).__name__}"
+        return
+    init_group("gloo", rank, world, timeout_s=30.0)
+    try:
+        if case == "bad_shape":
+            try:
+                agree_on_layer(dict(tokens=4096, n_head=16, n_head_kv=16,
+                                    head_dim=128 if rank == 0 else 64, world=world))
+                result[rank] = "agreed"
+            except ShardMismatch as e:
+                result[rank] = f"mismatch: {e}"
+        elif case == "rank_raises":
+            board = FailureBoard()
+            if rank == 1:
+                try:
+                    with board.step():
+                        raise RuntimeError("injected failure in step 0")
+                except RuntimeError:
+                    result[rank] = "raised"
+            else:
+                try:
+                    board.wait_for(1, 20.0)
+                    result[rank] = "no notice"
+                except RankFailed as e:
+                    result[rank] = f"saw rank {e.rank}: {e.what}"
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_failure_case(case):
+    world = 2
+    mgr = mp.Manager()
+    result = mgr.dict()
+    mp.spawn(_failure_worker, args=(world, _free_port(), case, result), nprocs=world, join=True)
+    return dict(result)
+
+
+def test_bad_shape_on_one_rank_is_an_error_on_every_rank():
+    res = _run_failure_case("bad_shape")
+    assert res[0].startswith("mismatch: layer arguments differ: head_dim = 128 here, 64 on rank 1")
+    assert res[1].startswith("mismatch: layer arguments differ: head_dim = 64 here, 128 on rank 0")
+
+
+def test_rank_that_raises_between_steps_is_seen_by_the_others():
+    res = _run_failure_case("rank_raises")
+    assert res[1] == "raised"
+    assert res[0] == "saw rank 1: RuntimeError: injected failure in step 0"
+
+
+def test_rank_that_never_joins_times_out_the_rendezvous():
+    res = _run_failure_case("never_joins")
+    assert res[1] == "stayed away"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2].rstrip("s:")) < 30.0
