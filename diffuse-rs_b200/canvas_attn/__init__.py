@@ -89,7 +89,7 @@ class CaDevArgs(ctypes.Structure):
                 ("scale", ctypes.c_float), ("softcap", ctypes.c_float),
                 ("precise", ctypes.c_int32), ("status", ctypes.c_void_p),
                 ("peer_out", ctypes.c_void_p), ("n_peer_out", ctypes.c_int32),
-                ("seq_prefix", ctypes.c_void_p)]
+                ("seq_prefix", ctypes.c_void_p), ("out_multicast", ctypes.c_void_p)]
 
 
 class CaBlockArgs(ctypes.Structure):
@@ -110,7 +110,8 @@ class CaBlockArgs(ctypes.Structure):
                 ("peer_out", ctypes.c_void_p), ("n_peer_out", ctypes.c_int32),
                 ("cu_active", ctypes.c_void_p), ("cu_total", ctypes.c_void_p),
                 ("max_active", ctypes.c_int32), ("total_active", ctypes.c_int64),
-                ("total_cache", ctypes.c_int64), ("seq_prefix", ctypes.c_void_p)]
+                ("total_cache", ctypes.c_int64), ("seq_prefix", ctypes.c_void_p),
+                ("out_multicast", ctypes.c_void_p)]
 
 
 def _load():
@@ -291,7 +292,8 @@ def make_dev_args(q, k, v, out, *, batch, sq, sk, n_head, n_head_kv, head_dim,
                   q_pos=None, k_pos=None, q_seq=None, k_seq=None, q_prefix=None,
                   sliding_window=None, causal_prefix=None, scale=1.0, softcap=0.0,
                   q_row_stride=0, kv_row_stride=0, out_row_stride=0,
-                  precise=False, status=None, peer_out=None, seq_prefix=None) -> CaDevArgs:
+                  precise=False, status=None, peer_out=None, seq_prefix=None,
+                  out_multicast=None) -> CaDevArgs:
     peers, n_peers = _peer_array(peer_out)
     a = CaDevArgs(_ptr(q), _ptr(k), _ptr(v), _ptr(out), 1 if out_f32 else 0,
                      q_row_stride, kv_row_stride, out_row_stride, batch, sq, sk,
@@ -302,7 +304,7 @@ def make_dev_args(q, k, v, out, *, batch, sq, sk, n_head, n_head_kv, head_dim,
                      -1 if causal_prefix is None else int(causal_prefix),
                      float(scale), float(softcap), 1 if precise else 0, _ptr(status),
                      ctypes.cast(peers, ctypes.c_void_p) if peers is not None else None, n_peers,
-                     _ptr(seq_prefix))
+                     _ptr(seq_prefix), out_multicast)
     a._keep = peers
     return a
 
@@ -323,7 +325,8 @@ def make_block_args(q, k, v, *, batch, n_active, active_pos, rope, rope_len, rop
                     out_f32=False, sliding_window=None, causal_prefix=None, scale=1.0,
                     softcap=0.0, precise=False, status=None, out_row_stride=0,
                     peer_out=None, cu_active=None, cu_total=None, max_active=0,
-                    total_active=0, total_cache=0, seq_prefix=None) -> CaBlockArgs:
+                    total_active=0, total_cache=0, seq_prefix=None,
+                    out_multicast=None) -> CaBlockArgs:
     peers, n_peers = _peer_array(peer_out)
     a = CaBlockArgs(_ptr(q), _ptr(k), _ptr(v), batch, n_active, _ptr(active_pos),
                        _ptr(q_norm_w), _ptr(k_norm_w), 1 if v_norm else 0, float(rms_eps),
@@ -334,7 +337,7 @@ def make_block_args(q, k, v, *, batch, n_active, active_pos, rope, rope_len, rop
                        float(softcap), 1 if precise else 0, _ptr(status), int(out_row_stride),
                        ctypes.cast(peers, ctypes.c_void_p) if peers is not None else None,
                        n_peers, _ptr(cu_active), _ptr(cu_total), int(max_active),
-                       int(total_active), int(total_cache), _ptr(seq_prefix))
+                       int(total_active), int(total_cache), _ptr(seq_prefix), out_multicast)
     a._keep = peers
     return a
 

@@ -119,6 +119,62 @@ class PeerRows:
         self.peers = []
 
 
+class MulticastRows:
+    """Receive buffers of a head-sharded layer written through NVLink multicast.
+
+    Each rank allocates its [tokens, n_head, head_dim] buffer from torch's
+    symmetric memory, which binds the same-offset buffers of every rank to
+    one NVLS multicast object (plumbing only: the writes are the attention
+    epilogue's own multimem stores). A rank runs its attention with `out` =
+    its head slice of its buffer and `out_multicast` = the multicast address
+    of that slice: every output row crosses this GPU's NVLink once and the
+    switch writes it into every rank's buffer, where PeerRows sends it once
+    per peer. After a barrier every rank holds the full rows o_proj consumes
+    (src/model/forward.rs:345).
+
+    `available` is False (and `why` says why) when the box, driver or torch
+    build offers no multicast; callers then fall back to PeerRows or NCCL.
+    """
+
+    def __init__(self, tokens: int, n_head: int, head_dim: int, dtype=None, group=None):
+        import torch
+        import torch.distributed as dist
+        self.n_head, self.head_dim = n_head, head_dim
+        self.rank = dist.get_rank(group)
+        self.available, self.why, self.mc = False, "", 0
+        dtype = dtype or torch.bfloat16
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            grp = group if group is not None else dist.group.WORLD
+            name = grp.group_name
+            self.buf = symm_mem.empty((tokens, n_head, head_dim), dtype=dtype,
+                                      device=torch.device("cuda", torch.cuda.current_device()))
+            self.handle = symm_mem.rendezvous(self.buf, name)
+            mc = int(self.handle.multicast_ptr or 0)  # 0: no multicast object
+            base = int(self.handle.buffer_ptrs[self.rank])
+            off = self.buf.data_ptr() - base
+            nbytes = self.buf.numel() * self.buf.element_size()
+            if mc == 0:
+                self.why = "no NVLS multicast support on this box"
+            elif off < 0 or off + nbytes > int(self.handle.buffer_size) or mc % 16 or off % 16:
+                self.why = "buffer outside its symmetric allocation"
+            else:
+                self.mc = mc + off
+                self.available = True
+        except Exception as e:  # noqa: BLE001 - reported, never fatal
+            self.why = f"symmetric memory unavailable: {type(e).__name__}: {e}"
+        if not self.available and not hasattr(self, "buf"):
+            self.buf = torch.empty((tokens, n_head, head_dim), dtype=dtype, device="cuda")
+
+    def slice_args(self, shard: HeadShard):
+        """Output view, multicast address and out_row_stride of query heads
+        [q_begin, q_end)."""
+        esz = self.buf.element_size()
+        off = shard.q_begin * self.head_dim * esz
+        out = self.buf[:, shard.q_begin:shard.q_end]
+        return out, self.mc + off, self.n_head * self.head_dim
+
+
 # ---------------------------------------------------------------- failures
 # Host-side failure detection for multi-rank layers. The reference has no
 # multi-process path (its failure handling is request-level); these helpers

@@ -80,6 +80,11 @@ struct FwdParams {
   // [tokens, n_head, head_dim] buffer as the tiles finish.
   void* peer_out[kMaxPeers];
   int n_peer;
+  // NVLink multicast address bound to `out` on every rank (same offsets):
+  // the uniform-batch epilogue writes the staged tile through it with
+  // multimem stores instead of storing to `out` (the switch delivers each
+  // row to every rank's buffer, this one's included).
+  void* mc_out;
 };
 
 // Softmax organisation of a CTA (see the file comment):
@@ -1294,7 +1299,31 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         }
       }
     }
-    if (p.tma_out) {
+    if (p.tma_out && p.mc_out) {
+      // Multicast output: every softmax thread copies 16-byte units of the
+      // staged tile to the multicast address, consecutive threads along a
+      // row (a row of the tile is contiguous in `out`), so each warp writes
+      // whole 128-byte lines. The switch replicates each store to every
+      // rank's buffer: one crossing of this GPU's NVLink per row.
+      named_bar_sync(2, C::kSoftThreads);
+      const int es = p.out_f32 ? 4 : 2;
+      const int inner = 128 / es;                 // elements per staged chunk
+      const int upr = (C::HDO * es) / 16;         // 16-byte units per row
+      const int q_beg_u = b * p.sq;
+      const int tid_s = (warp - 3) * 32 + lane;
+      for (int u = tid_s; u < p.R * upr; u += C::kSoftThreads) {
+        const int rr = u / upr, cu = u % upr;     // tile row, unit within the row
+        const int ci = cu >> 3, uu = cu & 7;      // staged chunk, unit within it
+        const int tl = t0 + rr / p.G;
+        const int col = ocol + ci * inner + uu * (16 / es);
+        if (tl >= q_len || col >= p.hd) continue;
+        const uint4 w = *reinterpret_cast<const uint4*>(
+            smem + C::kOffStage + ci * C::kStageChunk + rr * 128 + ((uu ^ (rr & 7)) << 4));
+        const int64_t off = (static_cast<int64_t>(q_beg_u + tl) * p.out_row_stride +
+                             static_cast<int64_t>(kvh * p.G + rr % p.G) * p.hd + col) * es;
+        multimem_st_v4(static_cast<uint8_t*>(p.mc_out) + off, w);
+      }
+    } else if (p.tma_out) {
       // All softmax warps have staged their rows: one thread stores the tile.
       fence_proxy_async_smem();
       named_bar_sync(2, C::kSoftThreads);

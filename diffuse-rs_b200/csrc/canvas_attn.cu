@@ -123,6 +123,7 @@ struct Launch {
                       p->out_f32 != 0, p->G, p->QT) != CA_OK)
       pl.tma_out = 0;
     if (!pl.tma_out) to = tq;  // unused
+    if (pl.mc_out && !pl.tma_out) return CA_ERR_UNSUPPORTED;
     // Peer buffers: tensor maps of the same shape for the TMA epilogue;
     // the row-store epilogue writes them with plain stores instead.
     PeerMaps pm;
@@ -252,6 +253,10 @@ int attention_dev_impl(const ca_dev_args* a, cudaStream_t st, const QFuse* fq = 
     if (!a->peer_out[i] || !aligned16(a->peer_out[i])) return CA_ERR_INVALID;
     p.peer_out[i] = a->peer_out[i];
   }
+  // Multicast output: one multimem store per row reaches every rank's
+  // buffer (uniform batches, which stage the tile for the store pass).
+  p.mc_out = a->out_multicast;
+  if (p.mc_out && (a->cu_q || p.n_peer > 0 || !aligned16(p.mc_out))) return CA_ERR_INVALID;
   p.fuse_q = fq != nullptr;
   p.fq_w = fq ? fq->w : nullptr;
   p.fq_rope = fq ? fq->rope : nullptr;
@@ -474,6 +479,7 @@ int block_impl(const ca_block_args* a, cudaStream_t st) {
   d.out_row_stride = a->out_row_stride;
   d.peer_out = a->peer_out;
   d.n_peer_out = a->n_peer_out;
+  d.out_multicast = a->out_multicast;
   d.batch = a->batch;
   d.sq = a->n_active;
   d.sk = a->n_total;

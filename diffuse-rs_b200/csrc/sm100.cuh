@@ -286,6 +286,16 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn, i
 }
 
 // ---------------------------------------------------------------- math
+// One 16-byte store through an NVLink multicast address (multimem, PTX
+// ISA 8.1+): every GPU bound to the multicast object receives it. The bits
+// are stored unchanged (the .f32 vector type only sizes the access).
+__device__ __forceinline__ void multimem_st_v4(void* mc_addr, uint4 w) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr),
+               "f"(__uint_as_float(w.x)), "f"(__uint_as_float(w.y)), "f"(__uint_as_float(w.z)),
+               "f"(__uint_as_float(w.w))
+               : "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

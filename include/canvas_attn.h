@@ -129,6 +129,14 @@ typedef struct {
                                   (Gemma's per-sequence canvas_start, forward.rs:153-160),
                                   negative = None; used when q_prefix is NULL and
                                   overrides causal_prefix */
+    void* out_multicast;     /* optional NVLink multicast address (an NVLS multicast
+                                  object, e.g. torch symmetric memory's multicast_ptr)
+                                  bound to `out` on every rank of a head-sharded group,
+                                  at the same offset as `out`: the epilogue writes each
+                                  finished row once through it (multimem.st) and the
+                                  switch delivers it to every rank's buffer, this one's
+                                  included. Uniform batches only; peer_out must be
+                                  empty. NULL = off */
 } ca_dev_args;
 #define CA_MAX_PEERS 7
 
@@ -190,6 +198,7 @@ typedef struct {
     int64_t total_active;      /* varlen: cu_active[batch] */
     int64_t total_cache;       /* varlen: cu_total[batch] */
     const int32_t* seq_prefix; /* as ca_dev_args.seq_prefix */
+    void* out_multicast;       /* as ca_dev_args.out_multicast */
 } ca_block_args;
 
 /*
