@@ -396,6 +396,12 @@ class E2E:
         self.calls = len(c["layers"]) * c["B"]
         self.h2d = self.calls * 4 * (self.q.size + self.k.size + self.v.size)
         self.d2h = self.calls * 4 * self.out.size
+        # Calls of at least 16 MiB of fp32 Q (head_dim a multiple of 8) run
+        # pipelined, with Q/K/V rounded to bf16 on host threads before the
+        # copies (CA_HOST_ROUND=0 turns that off): half the bytes cross PCIe.
+        piped = self.q.size * 4 >= (16 << 20) and c["hd"] % 8 == 0 and nk > 0
+        hround = os.environ.get("CA_HOST_ROUND", "1") != "0"
+        self.pcie_h2d = self.h2d // 2 if piped and hround else self.h2d
 
     def step(self):
         c = self.cfg
@@ -899,7 +905,8 @@ def run_ours(args, cfg):
         dt = max_over_ranks(time.perf_counter() - t0, world)
         e2e = dict(value=round(world * flops * n_e2e / dt / 1e12, 3), unit="TFLOP/s",
                    h2d_bytes_per_step=ee.h2d, d2h_bytes_per_step=ee.d2h, steps=n_e2e,
-                   api="ca_attention_host_f32 (fp32 host buffers, precise weights)")
+                   api="ca_attention_host_f32 (fp32 host buffers, precise weights)",
+                   pcie_h2d_bytes_per_step=ee.pcie_h2d)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

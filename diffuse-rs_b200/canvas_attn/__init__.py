@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "ca_selftest_wait_timeout_status",
     "ca_status_string",
     "ca_version",
+    "ca_round_bf16_host",
 )
 
 
@@ -132,6 +133,8 @@ def _load():
     L.ca_build_rope_table.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                       ctypes.c_float, ctypes.c_void_p]
     L.ca_build_rope_table.restype = ctypes.c_int
+    L.ca_round_bf16_host.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64]
+    L.ca_round_bf16_host.restype = ctypes.c_int
     L.ca_device_status.argtypes = [ctypes.c_void_p]
     L.ca_device_status.restype = ctypes.c_int
     L.ca_selftest_wait_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p]
@@ -394,3 +397,13 @@ def selftest_wait_timeout_status(limit_ns: int, status, stream=None) -> None:
     device-wide word."""
     _check(lib.ca_selftest_wait_timeout_status(int(limit_ns), _ptr(status), _stream(stream)),
            "ca_selftest_wait_timeout_status")
+
+
+def round_bf16_host(x):
+    """ca_round_bf16_host: numpy float32 array -> numpy uint16 bf16 bit
+    patterns, rounded on the host as the host-buffer entry point does."""
+    import numpy as np
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    _check(lib.ca_round_bf16_host(x.ctypes.data, out.ctypes.data, x.size), "ca_round_bf16_host")
+    return out

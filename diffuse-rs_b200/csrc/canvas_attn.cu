@@ -10,8 +10,11 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <vector>
+
+#include "host_round.h"
 
 #include "canvas_attn.h"
 #include "attn_fwd.cuh"
@@ -519,8 +522,20 @@ struct HostCtx {
   cudaEvent_t ev[2 * kMaxChunks + 1] = {};
   void* buf = nullptr;
   size_t cap = 0;
+  uint16_t* pin = nullptr;  // pinned host staging of bf16-rounded Q/K/V
+  size_t pin_cap = 0;
 };
 HostCtx g_host[kMaxDevices];
+
+// Host rounding of the pipelined host-buffer calls (CA_HOST_ROUND=0 keeps
+// fp32 over PCIe and rounds on the GPU).
+bool host_round_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("CA_HOST_ROUND");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 size_t align_up(size_t x) { return (x + 255) / 256 * 256; }
 
@@ -641,30 +656,89 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
         return CA_ERR_CUDA;
     const int64_t row_e = s->n_head * hd;  // elements per query row
     const int64_t rows_per = (nq + n_chunks - 1) / n_chunks;
-    bool okp = cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess &&
-               cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess &&
-               cudaMemcpyAsync(dmeta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice,
+    // Q, K and V are rounded to bf16 by host threads into pinned staging
+    // and cross PCIe as bf16 (half the bytes; the copy engine then reads
+    // pinned memory directly), the next chunk being rounded while the
+    // current one is in flight. The rounding equals the GPU's, so the
+    // kernels see the same operands as with fp32 copies.
+    const size_t pin_need = static_cast<size_t>(2 * ke + qe) * 2;
+    bool hr = host_round_enabled();
+    if (hr && pin_need > c.pin_cap) {
+      if (c.pin) cudaFreeHost(c.pin);
+      c.pin = nullptr;
+      c.pin_cap = 0;
+      if (cudaHostAlloc(reinterpret_cast<void**>(&c.pin), pin_need, cudaHostAllocDefault) ==
+          cudaSuccess)
+        c.pin_cap = pin_need;
+      else
+        cudaGetLastError();  // fall back to fp32 copies
+    }
+    hr = hr && c.pin_cap >= pin_need;
+    uint16_t* pk = hr ? c.pin : nullptr;
+    uint16_t* pv = hr ? c.pin + ke : nullptr;
+    uint16_t* pq = hr ? c.pin + 2 * ke : nullptr;
+    // One rounding job for the whole call: K and V in pieces of at most 2M
+    // elements, then each Q chunk; a piece is copied as soon as it is rounded.
+    std::vector<RoundSeg> segs;
+    std::vector<__nv_bfloat16*> seg_dev;
+    int kv_segs = 0;
+    if (hr) {
+      constexpr int64_t kPiece = 1 << 21;
+      for (int t = 0; t < 2; ++t)
+        for (int64_t o = 0; o < ke; o += kPiece) {
+          segs.push_back({(t ? v : k) + o, (t ? pv : pk) + o,
+                          static_cast<size_t>(std::min(kPiece, ke - o))});
+          seg_dev.push_back((t ? hv : hk) + o);
+        }
+      kv_segs = static_cast<int>(segs.size());
+      for (int ch = 0; ch < n_chunks; ++ch) {
+        const int64_t r0 = ch * rows_per, rows = std::min<int64_t>(rows_per, nq - r0);
+        if (rows <= 0) break;
+        segs.push_back({q + r0 * row_e, pq + r0 * row_e, static_cast<size_t>(rows * row_e)});
+        seg_dev.push_back(hq + r0 * row_e);
+      }
+    }
+    std::unique_ptr<RoundBatch> rb(hr ? new RoundBatch(segs.data(), static_cast<int>(segs.size()))
+                                      : nullptr);
+    bool okp = cudaMemcpyAsync(dmeta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice,
                                st) == cudaSuccess;
+    if (hr) {
+      for (int i = 0; i < kv_segs; ++i) {
+        rb->wait(i);
+        okp = okp && cudaMemcpyAsync(seg_dev[i], segs[i].dst, segs[i].n * 2,
+                                     cudaMemcpyHostToDevice, st) == cudaSuccess;
+      }
+    } else {
+      okp = okp && cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+            cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    }
     if (okp && qseq != kseq) okp = cudaMemsetAsync(dzero, 0, 4 * (nq + nk), st) == cudaSuccess;
     okp = okp && cudaMemsetAsync(dstatus, 0, 4, st) == cudaSuccess;
     okp = okp && cudaEventRecord(c.ev[2 * kMaxChunks], st) == cudaSuccess &&
           cudaStreamWaitEvent(c.comp, c.ev[2 * kMaxChunks], 0) == cudaSuccess;
     if (!okp) return fail(CA_ERR_CUDA);
     const int kblocks = static_cast<int>(std::min<long long>((ke / 4 + 255) / 256 + 1, 148 * 8));
-    f32_to_bf16_kernel<<<kblocks, 256, 0, c.comp>>>(dk, hk, ke);
-    f32_to_bf16_kernel<<<kblocks, 256, 0, c.comp>>>(dv, hv, ke);
+    if (!hr) {
+      f32_to_bf16_kernel<<<kblocks, 256, 0, c.comp>>>(dk, hk, ke);
+      f32_to_bf16_kernel<<<kblocks, 256, 0, c.comp>>>(dv, hv, ke);
+    }
     for (int ch = 0; ch < n_chunks; ++ch) {
       const int64_t r0 = ch * rows_per;
       const int64_t rows = std::min<int64_t>(rows_per, nq - r0);
       if (rows <= 0) break;
       const int64_t e0 = r0 * row_e, n = rows * row_e;
       cudaEvent_t in_done = c.ev[2 * ch], att_done = c.ev[2 * ch + 1];
-      okp = cudaMemcpyAsync(dq + e0, q + e0, n * 4, cudaMemcpyHostToDevice, st) == cudaSuccess &&
-            cudaEventRecord(in_done, st) == cudaSuccess &&
+      if (hr) {
+        rb->wait(kv_segs + ch);
+        okp = cudaMemcpyAsync(hq + e0, pq + e0, n * 2, cudaMemcpyHostToDevice, st) == cudaSuccess;
+      } else {
+        okp = cudaMemcpyAsync(dq + e0, q + e0, n * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+      }
+      okp = okp && cudaEventRecord(in_done, st) == cudaSuccess &&
             cudaStreamWaitEvent(c.comp, in_done, 0) == cudaSuccess;
       if (!okp) return fail(CA_ERR_CUDA);
       const int qblocks = static_cast<int>(std::min<long long>((n / 4 + 255) / 256 + 1, 148 * 8));
-      f32_to_bf16_kernel<<<qblocks, 256, 0, c.comp>>>(dq + e0, hq + e0, n);
+      if (!hr) f32_to_bf16_kernel<<<qblocks, 256, 0, c.comp>>>(dq + e0, hq + e0, n);
       if (cudaGetLastError() != cudaSuccess) return fail(CA_ERR_CUDA);
       ca_dev_args d{};
       d.q = hq + e0;
@@ -1165,6 +1239,13 @@ int ca_selftest_wait_timeout_status(int64_t limit_ns, int32_t* status, void* str
 
 int ca_attention_block_dev_noalloc(const ca_block_args* a, void* stream) {
   return ca::noalloc_impl(a, static_cast<cudaStream_t>(stream));
+}
+
+int ca_round_bf16_host(const float* src, uint16_t* dst, uint64_t n) {
+  if (n == 0) return CA_OK;
+  if (!src || !dst) return CA_ERR_INVALID;
+  ca::host_round_bf16(src, dst, static_cast<size_t>(n));
+  return CA_OK;
 }
 
 int ca_attention_host_f32(float* out, const float* q, const float* k, const float* v,

@@ -397,6 +397,15 @@ int ca_selftest_wait_timeout(int64_t limit_ns, void* stream);
  * afterwards *status holds CA_ERR_TIMEOUT and ca_device_status is unaffected. */
 int ca_selftest_wait_timeout_status(int64_t limit_ns, int32_t* status, void* stream);
 
+/* Host-side fp32 -> bf16 rounding that ca_attention_host_f32 applies to
+ * large calls before their host-to-device copies (no counterpart in the
+ * reference, whose operands stay fp32): round to nearest even, every NaN to
+ * 0x7FFF and overflow to infinity, the GPU's cvt.rn.bf16.f32, so the kernels
+ * see the same operands as when they round on the device. Runs on a pool of
+ * host threads; dst receives n bf16 bit patterns. Returns CA_ERR_INVALID for
+ * null pointers with n > 0. */
+int ca_round_bf16_host(const float* src, uint16_t* dst, uint64_t n);
+
 /* Human-readable text of a ca_status. */
 const char* ca_status_string(int status);
 

@@ -92,3 +92,27 @@ def test_selftest_rejects_bad_limits_without_launching():
     assert ca.lib.ca_selftest_wait_timeout(0, None) == ca.CA_ERR_INVALID
     assert ca.lib.ca_selftest_wait_timeout(-5, None) == ca.CA_ERR_INVALID
     assert ca.lib.ca_selftest_wait_timeout(2_000_000_000, None) == ca.CA_ERR_INVALID
+
+
+def test_host_bf16_rounding_is_round_to_nearest_even():
+    """ca_round_bf16_host (the rounding the host-buffer entry point applies
+    before its copies) against torch's round-to-nearest-even on the CPU:
+    ties, values just below and above ties, subnormals, the overflow edge,
+    infinities; every NaN becomes 0x7FFF (what cvt.rn.bf16.f32 gives)."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(3)
+    bits = rng.integers(0, 2**32, size=1_000_003, dtype=np.uint64).astype(np.uint32)
+    edge = np.array([0x3f808000, 0x3f818000, 0x3f807fff, 0x3f808001, 0x00000001, 0x00008000,
+                     0x00018000, 0x7f7fffff, 0x7f7f8000, 0x7f7f7fff, 0xff7fffff, 0x7f800000,
+                     0xff800000, 0x00000000, 0x80000000, 0x7fc00000, 0xffc00001, 0x7f800001],
+                    dtype=np.uint32)
+    bits = np.concatenate([edge, bits])
+    x = bits.view(np.float32)
+    got = ca.round_bf16_host(x)
+    want = torch.from_numpy(x.copy()).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    nan = np.isnan(x)
+    assert np.array_equal(got[~nan], want[~nan])
+    assert np.all(got[nan] == 0x7FFF)
+    # Small calls (one task on the calling thread) round the same way.
+    assert np.array_equal(ca.round_bf16_host(x[:1000]), got[:1000])
