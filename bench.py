@@ -396,12 +396,15 @@ class E2E:
         self.calls = len(c["layers"]) * c["B"]
         self.h2d = self.calls * 4 * (self.q.size + self.k.size + self.v.size)
         self.d2h = self.calls * 4 * self.out.size
-        # Calls of at least 16 MiB of fp32 Q (head_dim a multiple of 8) run
-        # pipelined, with Q/K/V rounded to bf16 on host threads before the
-        # copies (CA_HOST_ROUND=0 turns that off): half the bytes cross PCIe.
-        piped = self.q.size * 4 >= (16 << 20) and c["hd"] % 8 == 0 and nk > 0
+        # Calls of at least 4 MiB of bf16 operands (or 16 MiB of fp32 Q, the
+        # pipelined form), head_dim a multiple of 8, round Q/K/V to bf16 on
+        # host threads before the copies (CA_HOST_ROUND=0 turns that off):
+        # half the bytes cross PCIe.
+        big = (self.q.size * 4 >= (16 << 20) or
+               (self.q.size + self.k.size + self.v.size) * 2 >= (4 << 20))
+        rounded = big and c["hd"] % 8 == 0 and nk > 0
         hround = os.environ.get("CA_HOST_ROUND", "1") != "0"
-        self.pcie_h2d = self.h2d // 2 if piped and hround else self.h2d
+        self.pcie_h2d = self.h2d // 2 if rounded and hround else self.h2d
 
     def step(self):
         c = self.cfg

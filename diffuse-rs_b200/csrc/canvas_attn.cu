@@ -776,9 +776,40 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
       return fail(CA_ERR_CUDA);
     return call_status();
   }
-  bool ok = cudaMemcpyAsync(dq, q, qe * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
-  ok = ok && (ke == 0 || cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess);
-  ok = ok && (ke == 0 || cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) == cudaSuccess);
+  // Calls of a few MB and up without head_dim padding round on the host too
+  // (see the pipelined form): one job, each of Q, K, V copied once rounded.
+  const size_t one_pin = static_cast<size_t>(qe + 2 * ke) * 2;
+  bool hr1 = host_round_enabled() && hd_p == hd && ke > 0 && one_pin >= (4u << 20);
+  if (hr1 && one_pin > c.pin_cap) {
+    if (c.pin) cudaFreeHost(c.pin);
+    c.pin = nullptr;
+    c.pin_cap = 0;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&c.pin), one_pin, cudaHostAllocDefault) ==
+        cudaSuccess)
+      c.pin_cap = one_pin;
+    else
+      cudaGetLastError();
+  }
+  hr1 = hr1 && c.pin_cap >= one_pin;
+  bool ok = true;
+  if (hr1) {
+    const RoundSeg segs[3] = {{k, c.pin, static_cast<size_t>(ke)},
+                              {v, c.pin + ke, static_cast<size_t>(ke)},
+                              {q, c.pin + 2 * ke, static_cast<size_t>(qe)}};
+    __nv_bfloat16* devs[3] = {hk, hv, hq};
+    RoundBatch rb(segs, 3);
+    for (int i = 0; i < 3; ++i) {
+      rb.wait(i);
+      ok = ok && cudaMemcpyAsync(devs[i], segs[i].dst, segs[i].n * 2, cudaMemcpyHostToDevice,
+                                 st) == cudaSuccess;
+    }
+  } else {
+    ok = cudaMemcpyAsync(dq, q, qe * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    ok = ok && (ke == 0 || cudaMemcpyAsync(dk, k, ke * 4, cudaMemcpyHostToDevice, st) ==
+                               cudaSuccess);
+    ok = ok && (ke == 0 || cudaMemcpyAsync(dv, v, ke * 4, cudaMemcpyHostToDevice, st) ==
+                               cudaSuccess);
+  }
   ok = ok && cudaMemcpyAsync(dmeta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, st) ==
                  cudaSuccess;
   if ((qseq != kseq) && ok)
@@ -792,10 +823,12 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
     else
       f32_to_bf16_pad_kernel<<<blocks, 256, 0, st>>>(src, dst, n / hd, hd, hd_p);
   };
-  conv(dq, hq, qe, qe_p);
-  if (ke > 0) {
-    conv(dk, hk, ke, ke_p);
-    conv(dv, hv, ke, ke_p);
+  if (!hr1) {
+    conv(dq, hq, qe, qe_p);
+    if (ke > 0) {
+      conv(dk, hk, ke, ke_p);
+      conv(dv, hv, ke, ke_p);
+    }
   }
   if (cudaGetLastError() != cudaSuccess) return CA_ERR_CUDA;
   ca_dev_args d{};

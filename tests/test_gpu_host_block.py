@@ -352,3 +352,31 @@ def test_block_varlen_block_diagonal_batch(hd, qk_norm, v_norm, gemma):
     ref = oracle_attention(qq, kk, vv, nq=n, nk=n, h=H, hkv=Hkv, hd=hd, q_pos=pos, k_pos=pos,
                            q_seq=seq, k_seq=seq, q_prefix=prefix, scale=scale)
     check_close(out.cpu().numpy(), ref, H, hd, what=f"varlen block hd={hd} gemma={gemma}")
+
+
+@pytest.mark.parametrize("n, nk, H, Hkv", [(4096, 4096, 8, 2), (32, 4128, 32, 8)])
+def test_host_entry_rounds_operands_like_the_device(n, nk, H, Hkv):
+    # Raw fp32 operands (not bf16-representable): large host calls round them
+    # to bf16 on host threads before copying (the pipelined form at 4096
+    # queries, the one-shot form for a c4-shaped call of 32 queries over
+    # 4128 keys). The rounding must be the device's round-to-nearest-even, so
+    # the output equals, bit for bit, the output for the same operands
+    # rounded by torch beforehand; and it matches the oracle on those.
+    rng = np.random.default_rng(11)
+    hd = 128
+    q = (rng.standard_normal(n * H * hd) * 3).astype(np.float32)
+    k = (rng.standard_normal(nk * Hkv * hd) * 3).astype(np.float32)
+    v = rng.standard_normal(nk * Hkv * hd).astype(np.float32)
+    rnd = lambda x: bf16_round(torch.from_numpy(x)).numpy()  # noqa: E731
+    s = ca.AttnShape(n, nk, H, Hkv, hd, scale=hd ** -0.5 / 3)
+    qr, kr = ca.Rows(np.arange(nk - n, nk)), ca.Rows(np.arange(nk))
+    out_raw = np.full(n * H * hd, np.inf, np.float32)
+    out_pre = np.full(n * H * hd, np.inf, np.float32)
+    ca.attention(out_raw, q, k, v, s, qr, kr)
+    ca.attention(out_pre, rnd(q), rnd(k), rnd(v), s, qr, kr)
+    assert np.array_equal(out_raw, out_pre)
+    ref = orc.attention(rnd(q), rnd(k), rnd(v), nq=n, nk=nk, n_head=H, n_head_kv=Hkv,
+                        head_dim=hd, scale=hd ** -0.5 / 3, q_pos=np.arange(nk - n, nk),
+                        k_pos=np.arange(nk),
+                        kind=orc.ROW_AVX2 if orc.have_avx2() else orc.ROW_SCALAR)
+    check_close(out_raw, ref, H, hd, what="host-rounded operands")
