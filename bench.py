@@ -674,7 +674,7 @@ def run_head_sharded(args, cfg, world, rank, dev):
             rc = ca.lib.ca_attention_block_dev(ctypes.byref(a), wl.stream.cuda_stream)
             if rc != 0:
                 raise ca.CaError(rc, "ca_attention_block_dev (multicast rows)")
-        dist.all_reduce(flag)  # every rank's multicast stores are in place after this
+        mrecv[0].barrier(wl.stream)  # every rank's multicast stores are in place after this
 
     # --- NCCL form
     n_chunks = max(1, min(args.hs_chunks, B))
@@ -777,7 +777,8 @@ def run_head_sharded(args, cfg, world, rank, dev):
     mc_line = (dict(value=tf(t_mc), ms_per_step=round(t_mc / args.steps, 4),
                     gather="attention epilogue writes each row once through an NVLS "
                            "multicast address (multimem.st); the switch delivers it to "
-                           "every rank's buffer")
+                           "every rank's buffer",
+                    barrier="symmetric-memory signal-pad barrier on the stream")
                if mc_ok else dict(unavailable=mc_why))
     best = min(t for t in (t_peer, t_mc) if t is not None)
     return dict(value=tf(best), unit="TFLOP/s", compute_only=tf(comp),
@@ -787,7 +788,7 @@ def run_head_sharded(args, cfg, world, rank, dev):
                           gather="attention epilogue stores its tiles into every rank's "
                                  "receive buffer over NVLink (CUDA IPC peer mappings)"),
                 multicast=mc_line,
-                barrier="one stream-ordered 4-byte all_reduce per step",
+                barrier="peer and NCCL forms: one stream-ordered 4-byte all_reduce per step",
                 compute_ms_per_step=round(comp / args.steps, 4),
                 nccl=dict(value=tf(t_nccl), ms_per_step=round(t_nccl / args.steps, 4),
                           chunks=n_chunks,
