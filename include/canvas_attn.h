@@ -146,7 +146,7 @@ typedef struct {
  * asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream).
  * Batch is a grid dimension; varlen segments stand for the reference's
  * concatenated block-diagonal rows (src/model/forward.rs:113-160).
- * Allocates nothing. head_dim must be a multiple of 8 and <= 256.
+ * Allocates nothing. head_dim must be a multiple of 8 and <= 512.
  */
 int ca_attention_dev(const ca_dev_args* a, void* stream);
 
