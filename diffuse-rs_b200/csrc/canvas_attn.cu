@@ -637,7 +637,7 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
   const int64_t q_bytes = qe * 4;
   const int n_chunks =
       (hd_p == hd && nk > 0 && q_bytes >= (16ll << 20))
-          ? static_cast<int>(std::min<int64_t>(kMaxChunks, std::max<int64_t>(2, q_bytes >> 23)))
+          ? static_cast<int>(std::min<int64_t>(kMaxChunks, std::max<int64_t>(2, q_bytes >> 22)))
           : 1;
   if (n_chunks > 1) {
     // On an error, drain what was queued so the next call cannot overlap it.
@@ -683,7 +683,7 @@ int host_f32_impl(float* out, const float* q, const float* k, const float* v, co
     std::vector<__nv_bfloat16*> seg_dev;
     int kv_segs = 0;
     if (hr) {
-      constexpr int64_t kPiece = 1 << 21;
+      constexpr int64_t kPiece = 1 << 20;
       for (int t = 0; t < 2; ++t)
         for (int64_t o = 0; o < ke; o += kPiece) {
           segs.push_back({(t ? v : k) + o, (t ? pv : pk) + o,
